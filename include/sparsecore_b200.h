@@ -1,0 +1,196 @@
+/*
+ * sparsecore_b200 — C-ABI of the B200 (sm_100a) padded-CSR sparse-training
+ * kernels.
+ *
+ * Every entry point takes plain device pointers and sizes, enqueues its work
+ * on the CUDA stream passed as `stream` (a cudaStream_t passed as void*;
+ * NULL = legacy default stream) and returns 0 on success or a nonzero
+ * SL_ERR_* code, with a human-readable message in sl_last_error() (per
+ * thread).  Nothing here synchronises the device unless stated.
+ *
+ * Layout (identical to the reference's sparselab::PaddedCSR,
+ * csrc/kernels/padded_csr.hpp:47-74):
+ *   values       float[total_capacity]   live slots first in each row
+ *   col_indices  int32[total_capacity]   ascending within a row; padding -1
+ *   row_start    int32[nrows]            exclusive prefix sum of row_capacity
+ *   row_nnz      int32[nrows]
+ *   row_capacity int32[nrows]
+ * Dense operands are row-major float32: X[K,N], Y[M,N], dY[M,N].
+ */
+#ifndef SPARSECORE_B200_H
+#define SPARSECORE_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SL_API __attribute__((visibility("default")))
+#else
+#define SL_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    SL_OK = 0,
+    SL_ERR_INVALID = 1,     /* bad shape / argument (reference: ValueError) */
+    SL_ERR_CUDA = 2,        /* a CUDA runtime call failed                   */
+    SL_ERR_UNSUPPORTED = 3, /* size beyond a documented kernel limit        */
+    SL_ERR_TIMEOUT = 4      /* a bounded device-side wait ran out           */
+};
+
+/* Device-resident padded CSR (all pointers are device pointers). */
+typedef struct sl_csr {
+    int64_t nrows;
+    int64_t ncols;
+    int64_t total_capacity;
+    float* values;
+    int32_t* col_indices;
+    int32_t* row_start;
+    int32_t* row_nnz;
+    int32_t* row_capacity;
+} sl_csr;
+
+/* Message of the last failed call on this host thread ("" if none). */
+SL_API const char* sl_last_error(void);
+/* Library version string. */
+SL_API const char* sl_version(void);
+
+/* ── Forward SpMM ─────────────────────────────────────────────────────────
+ * Y[M,N] = W[M,K] . X[K,N].  Each Y element is the fp32 FMA chain over the
+ * row's live slots in slot order, starting from +0 — bit-identical to the
+ * reference CPU kernel.
+ * Replaces: csrc/kernels/spmm_avx2.cpp:82 spmm_simd_avx2 (and spmm_scalar,
+ * csrc/kernels/spmm.cpp:122) behind csrc/bindings.cpp:253 py_spmm_simd.
+ * Also computes dX = W^T . dY when given the transposed CSR
+ * (sparselab/ops.py:201-203). */
+SL_API int sl_spmm_fwd(const sl_csr* W, const float* X, int64_t K, int64_t N,
+                float* Y, void* stream);
+
+/* ── SDDMM weight gradient ────────────────────────────────────────────────
+ * dW[slot] = <dY[i,:], X[col[slot],:]> for live slots of row i, 0 for
+ * padding; dW has total_capacity entries aligned with W.values.  The dot is
+ * evaluated in the reference AVX2 kernel's lane order (bit-identical).
+ * Replaces: csrc/kernels/spmm_grad_avx2.cpp:73 spmm_grad_w_simd behind
+ * csrc/bindings.cpp:410 py_spmm_grad_w_simd. */
+SL_API int sl_sddmm_dw(const sl_csr* W, const float* dY, const float* X,
+                int64_t N, float* dW, void* stream);
+
+/* ── Transpose with permutation ───────────────────────────────────────────
+ * Two-phase GPU build of W^T (sparselab/layout.py:460 transpose_with_perm).
+ * Phase 1 counts: fills out_row_nnz/out_row_capacity/out_row_start (int32
+ * [ncols]) and *out_total_dev (device int64) with the transpose's total
+ * capacity, using `scratch` (device, sl_transpose_scratch_bytes bytes).
+ * Capacity per row = max(1, ceil(nnz * one_plus_padding_ratio)) in float64.
+ * Phase 2 fills WT (whose row arrays are the phase-1 outputs and whose slot
+ * arrays hold *out_total_dev entries) and perm[int64, WT total capacity]:
+ * perm[slot_T] = source slot in W, -1 for padding.  Output rows list the
+ * source rows in ascending order.  `scratch` must be passed unchanged from
+ * phase 1. */
+SL_API int64_t sl_transpose_scratch_bytes(int64_t nrows, int64_t ncols);
+SL_API int sl_transpose_count(const sl_csr* W, double one_plus_padding_ratio,
+                       int32_t* out_row_nnz, int32_t* out_row_capacity,
+                       int32_t* out_row_start, int64_t* out_total_dev,
+                       void* scratch, void* stream);
+SL_API int sl_transpose_fill(const sl_csr* W, const sl_csr* WT, int64_t* perm,
+                      const void* scratch, void* stream);
+
+/* Cached-transpose value refresh: dst[t] = src[perm[t]] where perm[t] >= 0
+ * (sparselab/ops.py:83-94, the cache-hit path of _cached_transpose). */
+SL_API int sl_values_gather(const int64_t* perm, const float* src, float* dst,
+                     int64_t n, void* stream);
+
+/* ── Layout factories ─────────────────────────────────────────────────────
+ * Dense [M,K] -> padded CSR (sparselab/layout.py:172 from_dense, via
+ * from_torch_sparse_csr :75).  live = |w| > threshold if threshold > 0,
+ * else w != 0.
+ * Phase 1: row_nnz, row_capacity, row_start and *out_total_dev.
+ * Phase 2: fill values/col_indices of `out` (sized from phase 1). */
+SL_API int sl_dense_count(const float* dense, int64_t M, int64_t K, float threshold,
+                   double one_plus_padding_ratio, int32_t* row_nnz,
+                   int32_t* row_capacity, int32_t* row_start,
+                   int64_t* out_total_dev, void* stream);
+SL_API int sl_dense_fill(const float* dense, float threshold, const sl_csr* out,
+                  void* stream);
+/* Capacity + exclusive scan for given per-row counts (layout.py:46-68,
+ * :131-133). */
+SL_API int sl_capacity_scan(const int32_t* row_nnz, int64_t n,
+                     double one_plus_padding_ratio, int32_t* row_capacity,
+                     int32_t* row_start, int64_t* out_total_dev,
+                     void* stream);
+/* Padded CSR -> dense [M,K] (layout.py:262 to_dense); `dense` is fully
+ * overwritten. */
+SL_API int sl_to_dense(const sl_csr* W, float* dense, void* stream);
+
+/* Invariant check (csrc/kernels/padded_csr.cpp:79 check_invariants_str).
+ * report (device int64[4]) receives {code, row, slot, 0}; code 0 = all hold,
+ * else 3 (row_start), 4 (row_nnz range), 6 (live column), 7 (padding
+ * column) of the first violation in the reference's check order.
+ * Array-length checks (invariants 1, 2) are the caller's. */
+SL_API int sl_check_invariants(const sl_csr* W, int64_t n_slots, int64_t* report,
+                        void* stream);
+
+/* ── Dense gradient (RigL grow criterion) ─────────────────────────────────
+ * G[M,K] = dY[M,N] . X[K,N]^T in fp32, each element accumulated over N in
+ * the reference build's rounding sequence (bit-identical).  Replaces csrc/kernels/dense_grad.cpp:463 dense_grad behind
+ * csrc/bindings.cpp:445 py_dense_grad. */
+SL_API int sl_dense_grad(const float* dY, const float* X, int64_t M, int64_t K,
+                  int64_t N, float* G, void* stream);
+
+/* ── Dynamic-sparsity prune / regrow (sparselab/router.py) ───────────────
+ * sl_dst_threshold: k-th smallest |value| (1-based k) over all live slots,
+ *   exact (router.py:395-412, np.partition).  Writes the float to *thr_dev.
+ *   scratch: sl_dst_scratch_bytes() bytes of device memory.
+ * sl_dst_keep: per row, n_keep[i] = #{live |v| > thr} with the reference's
+ *   force-keep of the first max-|v| slot when none survives
+ *   (router.py:420-439); force_idx[i] = that slot offset or -1.
+ * sl_dst_apply_random: SET rewrite (router.py:441-478).  grow_offsets
+ *   [nrows+1] (exclusive scan) delimit, per row, the 0-based ranks drawn
+ *   on the host among the row's non-surviving columns in ascending order
+ *   (numpy Generator.choice(pool, n_grow, replace=False)).  Grown slots get
+ *   value 0; the row is rewritten column-sorted with (-1, 0) padding.
+ * sl_dst_apply_topk: RigL rewrite (router.py:641-733): grows the n_grow =
+ *   min(n_live - n_keep, ncols - n_keep) non-surviving columns of largest
+ *   |G[i,:]|.  Rows whose choice is not unique (ties at the cut, or NaN)
+ *   are left untouched and flagged in row_flag[i] = 1 for the caller to
+ *   resolve (then sl_dst_apply_cols); row_flag[i] = 0 otherwise.
+ * sl_dst_apply_cols: rewrite given rows with explicit grown columns:
+ *   grow_offsets[nrows+1] delimit per-row column lists; rows with
+ *   row_mask[i] == 0 are not touched.
+ * All apply kernels need ncols <= sl_dst_max_ncols(). */
+SL_API int64_t sl_dst_scratch_bytes(void);
+SL_API int64_t sl_dst_max_ncols(void);
+SL_API int sl_dst_threshold(const sl_csr* W, int64_t k, float* thr_dev,
+                     void* scratch, void* stream);
+SL_API int sl_dst_keep(const sl_csr* W, const float* thr_dev, int32_t* n_keep,
+                int32_t* force_idx, void* stream);
+SL_API int sl_dst_apply_random(const sl_csr* W, const float* thr_dev,
+                        const int32_t* force_idx, const int32_t* grow_offsets,
+                        const int32_t* grow_ranks, void* stream);
+SL_API int sl_dst_apply_topk(const sl_csr* W, const float* thr_dev,
+                      const int32_t* force_idx, const float* G,
+                      int32_t* row_flag, void* stream);
+SL_API int sl_dst_apply_cols(const sl_csr* W, const float* thr_dev,
+                      const int32_t* force_idx, const int32_t* row_mask,
+                      const int32_t* grow_offsets, const int32_t* grow_cols,
+                      void* stream);
+
+/* ── Data-parallel packing of live gradient slots ────────────────────────
+ * packed_offsets[nrows] = exclusive scan of row_nnz.  pack copies the live
+ * slots of src[total_capacity] into dst[nnz]; unpack scatters back into
+ * dst[total_capacity] and, when scale != 1, multiplies by `scale`
+ * (padding slots of dst are left as they are). */
+SL_API int sl_pack_live(const sl_csr* W, const int32_t* packed_offsets,
+                 const float* src, float* dst, void* stream);
+SL_API int sl_unpack_live(const sl_csr* W, const int32_t* packed_offsets,
+                   const float* src, float* dst, float scale, void* stream);
+/* Exclusive scan of int32 counts (n <= 2^31 total) into out[n];
+ * *total_dev (device int64) receives the sum. */
+SL_API int sl_exclusive_scan(const int32_t* counts, int64_t n, int32_t* out,
+                      int64_t* total_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SPARSECORE_B200_H */

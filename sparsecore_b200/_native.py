@@ -1,0 +1,127 @@
+"""ctypes binding of the sparsecore_b200 C ABI (include/sparsecore_b200.h).
+
+The CUDA library is the only compute path: there is no CPU fallback.  If the
+library is missing or no CUDA device is present, every compute entry point
+raises RuntimeError.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_lib", "libsparsecore_b200.so")
+
+SL_OK, SL_ERR_INVALID, SL_ERR_CUDA, SL_ERR_UNSUPPORTED, SL_ERR_TIMEOUT = 0, 1, 2, 3, 4
+
+P = ctypes.c_void_p
+I64 = ctypes.c_int64
+I32 = ctypes.c_int
+F32 = ctypes.c_float
+F64 = ctypes.c_double
+
+
+class SlCsr(ctypes.Structure):
+    """Mirror of `sl_csr` (device pointers)."""
+
+    _fields_ = [
+        ("nrows", I64),
+        ("ncols", I64),
+        ("total_capacity", I64),
+        ("values", P),
+        ("col_indices", P),
+        ("row_start", P),
+        ("row_nnz", P),
+        ("row_capacity", P),
+    ]
+
+
+# name -> (restype, argtypes); every symbol the header declares.
+SIGNATURES: dict[str, tuple] = {
+    "sl_last_error": (ctypes.c_char_p, []),
+    "sl_version": (ctypes.c_char_p, []),
+    "sl_spmm_fwd": (I32, [P, P, I64, I64, P, P]),
+    "sl_sddmm_dw": (I32, [P, P, P, I64, P, P]),
+    "sl_transpose_scratch_bytes": (I64, [I64, I64]),
+    "sl_transpose_count": (I32, [P, F64, P, P, P, P, P, P]),
+    "sl_transpose_fill": (I32, [P, P, P, P, P]),
+    "sl_values_gather": (I32, [P, P, P, I64, P]),
+    "sl_dense_count": (I32, [P, I64, I64, F32, F64, P, P, P, P, P]),
+    "sl_dense_fill": (I32, [P, F32, P, P]),
+    "sl_capacity_scan": (I32, [P, I64, F64, P, P, P, P]),
+    "sl_to_dense": (I32, [P, P, P]),
+    "sl_check_invariants": (I32, [P, I64, P, P]),
+    "sl_dense_grad": (I32, [P, P, I64, I64, I64, P, P]),
+    "sl_dst_scratch_bytes": (I64, []),
+    "sl_dst_max_ncols": (I64, []),
+    "sl_dst_threshold": (I32, [P, I64, P, P, P]),
+    "sl_dst_keep": (I32, [P, P, P, P, P]),
+    "sl_dst_apply_random": (I32, [P, P, P, P, P, P]),
+    "sl_dst_apply_topk": (I32, [P, P, P, P, P, P]),
+    "sl_dst_apply_cols": (I32, [P, P, P, P, P, P, P]),
+    "sl_pack_live": (I32, [P, P, P, P, P]),
+    "sl_unpack_live": (I32, [P, P, P, P, F32, P]),
+    "sl_exclusive_scan": (I32, [P, I64, P, P, P]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load the library without requiring a GPU (used by CPU-side tests)."""
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise RuntimeError(
+                        "sparsecore_b200: CUDA library not built (expected "
+                        f"{LIB_PATH}); run `python -m sparsecore_b200.build`. "
+                        "There is no CPU fallback.")
+                _lib = load_library()
+    return _lib
+
+
+def require_cuda(device: torch.device | None = None) -> torch.device:
+    if not torch.cuda.is_available():
+        raise RuntimeError(
+            "sparsecore_b200 requires a CUDA device (B200 / sm_100a); there is no CPU path.")
+    if device is None:
+        return torch.device("cuda", torch.cuda.current_device())
+    device = torch.device(device)
+    if device.type != "cuda":
+        raise RuntimeError(f"sparsecore_b200 tensors live on CUDA devices, got device={device}")
+    if device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    return device
+
+
+def stream_ptr(device: torch.device) -> P:
+    return P(torch.cuda.current_stream(device).cuda_stream)
+
+
+def ptr(t: torch.Tensor | None) -> P:
+    return P(t.data_ptr()) if t is not None else P(0)
+
+
+def check(rc: int, fn: str = "") -> None:
+    """Translate a C-ABI status into the reference's Python exceptions."""
+    if rc == SL_OK:
+        return
+    msg = (lib().sl_last_error() or b"").decode("utf-8", "replace") or fn
+    if rc == SL_ERR_INVALID:
+        raise ValueError(msg)
+    raise RuntimeError(msg)

@@ -1,0 +1,79 @@
+// Shared helpers for the sparsecore_b200 CUDA kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <climits>
+#include <cstdint>
+#include <string>
+
+#include "../../include/sparsecore_b200.h"
+
+namespace slb {
+
+// Per-host-thread error message behind sl_last_error().
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+// SL_OK, or SL_ERR_CUDA with the runtime's message prefixed by `what`.
+int cuda_status(cudaError_t e, const char* what);
+// SM count of the current device (cached per device).
+int num_sms();
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned16(const void* p) {
+    return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+// Checks shared by every entry point that takes an sl_csr.
+int check_csr(const sl_csr* W, const char* fn);
+// Grid size for warp-per-row kernels of 256 threads (8 warps per CTA).
+int row_grid(int64_t M);
+
+constexpr int kWarp = 32;
+
+__device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
+
+__device__ __forceinline__ int warp_inclusive_scan(int v) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane_id() >= o) v += t;
+    }
+    return v;
+}
+
+// Block-wide exclusive scan of one int per thread; `ws` is shared scratch of
+// NT/32 ints; *total receives the block sum.  Contains __syncthreads().
+template <int NT>
+__device__ __forceinline__ int block_exclusive_scan(int v, int* ws, int* total) {
+    constexpr int NW = NT / 32;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int inc = warp_inclusive_scan(v);
+    if (lane == 31) ws[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < NW ? ws[lane] : 0;
+        w = warp_inclusive_scan(w);
+        if (lane < NW) ws[lane] = w;
+    }
+    __syncthreads();
+    const int base = warp ? ws[warp - 1] : 0;
+    *total = ws[NW - 1];
+    __syncthreads();
+    return base + inc - v;
+}
+
+__device__ __forceinline__ int warp_sum(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+}  // namespace slb
+
+#define SL_RETURN_IF_LAUNCH_FAILED(what)                                   \
+    do {                                                                  \
+        cudaError_t e_ = cudaGetLastError();                              \
+        if (e_ != cudaSuccess) return ::slb::cuda_status(e_, what);       \
+    } while (0)

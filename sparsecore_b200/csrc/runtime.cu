@@ -1,0 +1,181 @@
+// Library plumbing: error reporting, device properties, generic scans and
+// the live-slot pack/unpack used by data-parallel gradient exchange.
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+
+namespace slb {
+
+thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return SL_OK;
+    return fail(SL_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int num_sms() {
+    static std::mutex mu;
+    static std::vector<int> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= static_cast<int>(cache.size())) cache.resize(dev + 1, 0);
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+            n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+int check_csr(const sl_csr* W, const char* fn) {
+    if (W == nullptr) return fail(SL_ERR_INVALID, std::string(fn) + ": W is NULL");
+    if (W->nrows < 0 || W->ncols < 0)
+        return fail(SL_ERR_INVALID, std::string(fn) + ": negative shape");
+    if (W->nrows > INT_MAX || W->ncols > INT_MAX || W->total_capacity > INT_MAX)
+        return fail(SL_ERR_UNSUPPORTED,
+                    std::string(fn) + ": sizes beyond int32 indexing are not supported");
+    if (W->nrows > 0 && (W->row_start == nullptr || W->row_nnz == nullptr ||
+                         W->row_capacity == nullptr))
+        return fail(SL_ERR_INVALID, std::string(fn) + ": NULL row array");
+    if (W->total_capacity > 0 && (W->values == nullptr || W->col_indices == nullptr))
+        return fail(SL_ERR_INVALID, std::string(fn) + ": NULL slot array");
+    return SL_OK;
+}
+
+// ── single-CTA exclusive scan over an int32 array (n up to a few million) ──
+constexpr int kScanThreads = 1024;
+
+__global__ void __launch_bounds__(kScanThreads)
+exclusive_scan_kernel(const int32_t* __restrict__ in, int64_t n, int32_t* __restrict__ out,
+                      int64_t* __restrict__ total) {
+    __shared__ int ws[kScanThreads / 32];
+    int64_t carry = 0;
+    for (int64_t base = 0; base < n; base += kScanThreads) {
+        const int64_t idx = base + threadIdx.x;
+        const int v = idx < n ? in[idx] : 0;
+        int tot;
+        const int ex = block_exclusive_scan<kScanThreads>(v, ws, &tot);
+        if (idx < n) out[idx] = static_cast<int32_t>(carry + ex);
+        carry += tot;
+    }
+    if (threadIdx.x == 0 && total) *total = carry;
+}
+
+// Capacity max(1, ceil(nnz * one_plus_pr)) in float64 (IEEE multiply and
+// ceil, same rounding as numpy in the reference), then exclusive scan.
+__global__ void __launch_bounds__(kScanThreads)
+capacity_scan_kernel(const int32_t* __restrict__ nnz, int64_t n, double one_plus_pr,
+                     int32_t* __restrict__ cap, int32_t* __restrict__ start,
+                     int64_t* __restrict__ total) {
+    __shared__ int ws[kScanThreads / 32];
+    int64_t carry = 0;
+    for (int64_t base = 0; base < n; base += kScanThreads) {
+        const int64_t idx = base + threadIdx.x;
+        int c = 0;
+        if (idx < n) {
+            double s = ceil(__dmul_rn(static_cast<double>(nnz[idx]), one_plus_pr));
+            if (s < 1.0) s = 1.0;
+            c = static_cast<int>(s);
+            cap[idx] = c;
+        }
+        int tot;
+        const int ex = block_exclusive_scan<kScanThreads>(c, ws, &tot);
+        if (idx < n) start[idx] = static_cast<int32_t>(carry + ex);
+        carry += tot;
+    }
+    if (threadIdx.x == 0 && total) *total = carry;
+}
+
+// ── live-slot pack / unpack (warp per row) ──
+__global__ void __launch_bounds__(256)
+pack_live_kernel(int M, const int32_t* __restrict__ row_start, const int32_t* __restrict__ row_nnz,
+                 const int32_t* __restrict__ off, const float* __restrict__ src,
+                 float* __restrict__ dst) {
+    const int warps = gridDim.x * 8;
+    for (int row = blockIdx.x * 8 + (threadIdx.x >> 5); row < M; row += warps) {
+        const int rs = row_start[row], nn = row_nnz[row], o = off[row];
+        for (int k = threadIdx.x & 31; k < nn; k += 32) dst[o + k] = src[rs + k];
+    }
+}
+
+__global__ void __launch_bounds__(256)
+unpack_live_kernel(int M, const int32_t* __restrict__ row_start,
+                   const int32_t* __restrict__ row_nnz, const int32_t* __restrict__ off,
+                   const float* __restrict__ src, float* __restrict__ dst, float scale) {
+    const int warps = gridDim.x * 8;
+    for (int row = blockIdx.x * 8 + (threadIdx.x >> 5); row < M; row += warps) {
+        const int rs = row_start[row], nn = row_nnz[row], o = off[row];
+        for (int k = threadIdx.x & 31; k < nn; k += 32) {
+            const float v = src[o + k];
+            dst[rs + k] = scale == 1.0f ? v : __fmul_rn(v, scale);
+        }
+    }
+}
+
+int row_grid(int64_t M) {
+    const int64_t want = (M + 7) / 8;
+    const int64_t cap = static_cast<int64_t>(num_sms()) * 16;
+    return static_cast<int>(want < cap ? (want > 0 ? want : 1) : cap);
+}
+
+}  // namespace slb
+
+using namespace slb;
+
+extern "C" {
+
+const char* sl_last_error(void) { return slb::g_last_error.c_str(); }
+
+const char* sl_version(void) { return "sparsecore_b200 0.1.0 (sm_100a)"; }
+
+int sl_exclusive_scan(const int32_t* counts, int64_t n, int32_t* out, int64_t* total_dev,
+                      void* stream) {
+    if (n < 0) return fail(SL_ERR_INVALID, "sl_exclusive_scan: negative n");
+    exclusive_scan_kernel<<<1, kScanThreads, 0, as_stream(stream)>>>(counts, n, out, total_dev);
+    SL_RETURN_IF_LAUNCH_FAILED("sl_exclusive_scan");
+    return SL_OK;
+}
+
+int sl_capacity_scan(const int32_t* row_nnz, int64_t n, double one_plus_padding_ratio,
+                     int32_t* row_capacity, int32_t* row_start, int64_t* out_total_dev,
+                     void* stream) {
+    if (n < 0) return fail(SL_ERR_INVALID, "sl_capacity_scan: negative n");
+    if (!(one_plus_padding_ratio >= 1.0))
+        return fail(SL_ERR_INVALID, "sl_capacity_scan: padding_ratio must be >= 0");
+    capacity_scan_kernel<<<1, kScanThreads, 0, as_stream(stream)>>>(
+        row_nnz, n, one_plus_padding_ratio, row_capacity, row_start, out_total_dev);
+    SL_RETURN_IF_LAUNCH_FAILED("sl_capacity_scan");
+    return SL_OK;
+}
+
+int sl_pack_live(const sl_csr* W, const int32_t* packed_offsets, const float* src, float* dst,
+                 void* stream) {
+    if (int rc = check_csr(W, "sl_pack_live")) return rc;
+    if (W->nrows == 0) return SL_OK;
+    pack_live_kernel<<<row_grid(W->nrows), 256, 0, as_stream(stream)>>>(
+        static_cast<int>(W->nrows), W->row_start, W->row_nnz, packed_offsets, src, dst);
+    SL_RETURN_IF_LAUNCH_FAILED("sl_pack_live");
+    return SL_OK;
+}
+
+int sl_unpack_live(const sl_csr* W, const int32_t* packed_offsets, const float* src, float* dst,
+                   float scale, void* stream) {
+    if (int rc = check_csr(W, "sl_unpack_live")) return rc;
+    if (W->nrows == 0) return SL_OK;
+    unpack_live_kernel<<<row_grid(W->nrows), 256, 0, as_stream(stream)>>>(
+        static_cast<int>(W->nrows), W->row_start, W->row_nnz, packed_offsets, src, dst, scale);
+    SL_RETURN_IF_LAUNCH_FAILED("sl_unpack_live");
+    return SL_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,151 @@
+"""Sparse ops: ``spmm`` and its autograd function, with the cached transpose.
+
+Mirrors ``sparselab/ops.py``:
+
+* ``_cached_transpose`` / ``_clear_transpose_cache`` (ops.py:66-104): W^T and
+  its slot permutation are rebuilt only when ``W.topology_version`` or the
+  shape changes; otherwise W^T's values are refreshed from W through the
+  permutation (one gather kernel).
+* ``_SpMMFunction`` (ops.py:127-210): forward Y = W.X (``sl_spmm_fwd``);
+  backward dW = SDDMM(dY, X) at live slots (``sl_sddmm_dw``) and
+  dX = W^T.dY (``sl_spmm_fwd`` on the cached transpose).
+* ``spmm(W, X, kernel=...)`` (ops.py:217-331): same validation and error
+  types; ``kernel`` accepts "auto" | "simd" | "scalar", all of which run the
+  one CUDA kernel.  X must be a CUDA tensor (a CPU X raises RuntimeError:
+  there is no CPU path).
+"""
+from __future__ import annotations
+
+import weakref
+
+import torch
+
+from . import _native as N
+from .layout import PaddedCSR, transpose_with_perm
+
+__all__ = ["spmm"]
+
+_VALID_KERNELS = ("auto", "simd", "scalar")
+
+# id(W) -> (topology_version, (nrows, ncols), WT, perm)
+_transpose_cache: dict[int, tuple] = {}
+
+
+def _drop_cache_entry(key: int) -> None:
+    _transpose_cache.pop(key, None)
+
+
+def _cached_transpose(W: PaddedCSR) -> PaddedCSR:
+    """W^T, rebuilt on topology change, value-refreshed otherwise."""
+    key = id(W)
+    ver = W.topology_version
+    shape = (int(W.nrows), int(W.ncols))
+    hit = _transpose_cache.get(key)
+    if hit is not None and hit[0] == ver and hit[1] == shape:
+        WT, perm = hit[2], hit[3]
+        n = int(perm.numel())
+        if n:
+            N.check(N.lib().sl_values_gather(N.ptr(perm), N.ptr(W.values), N.ptr(WT.values), n,
+                                             W._stream()), "_cached_transpose")
+        return WT
+    WT, perm = transpose_with_perm(W)
+    if hit is None:
+        # Drop the entry when W dies, so a recycled id() can never hit.
+        weakref.finalize(W, _drop_cache_entry, key)
+    _transpose_cache[key] = (ver, shape, WT, perm)
+    return WT
+
+
+def _clear_transpose_cache() -> None:
+    """Testing utility: clear all cache entries."""
+    _transpose_cache.clear()
+
+
+def _spmm_raw(W: PaddedCSR, X: torch.Tensor) -> torch.Tensor:
+    """Y = W.X on the CUDA kernel; X float32 contiguous on W's device."""
+    M = W.nrows
+    K, Ncol = X.shape
+    Y = torch.empty(M, Ncol, dtype=torch.float32, device=X.device)
+    N.check(N.lib().sl_spmm_fwd(W._abi_ref(), N.ptr(X), K, Ncol, N.ptr(Y), W._stream()),
+            "spmm_simd")
+    return Y
+
+
+def _sddmm_raw(W: PaddedCSR, dY: torch.Tensor, X: torch.Tensor) -> torch.Tensor:
+    """dW[total_capacity] at live slots (padding 0)."""
+    dW = torch.empty(W.total_capacity, dtype=torch.float32, device=dY.device)
+    N.check(N.lib().sl_sddmm_dw(W._abi_ref(), N.ptr(dY), N.ptr(X), dY.shape[1], N.ptr(dW),
+                                W._stream()), "spmm_grad_w_simd")
+    return dW
+
+
+def _check_dense(W: PaddedCSR, X: torch.Tensor, fn: str) -> torch.Tensor:
+    if X.device.type != "cuda":
+        raise RuntimeError(f"{fn}: X must be on a CUDA device (got device={X.device}). "
+                           f"sparsecore_b200 has no CPU path.")
+    if X.device != W.device:
+        raise RuntimeError(f"{fn}: X is on {X.device} but W is on {W.device}")
+    if X.dim() != 2:
+        raise ValueError(f"{fn}: X must be 2-D, got ndim={X.dim()}.")
+    if X.shape[0] != W.ncols:
+        raise ValueError(f"{fn}: shape mismatch. W has ncols={W.ncols} but X has "
+                         f"shape[0]={X.shape[0]}. Inner dimensions must match for matmul.")
+    return X.to(dtype=torch.float32).contiguous()
+
+
+class _SpMMFunction(torch.autograd.Function):
+    """Autograd wrapper for Y = W @ X with W a PaddedCSR.
+
+    Inputs ``(W_values, W, X, kernel)``; ``W_values`` is the tensor autograd
+    tracks (it aliases ``W.values``), ``W`` travels as metadata.  Backward
+    returns ``(dW_values[total_capacity], None, dX, None)``.
+    """
+
+    @staticmethod
+    def forward(ctx, W_values, W, X, kernel):
+        X_c = _check_dense(W, X, "spmm_simd")
+        ctx.save_for_backward(W_values, X_c)
+        ctx.W = W
+        ctx.kernel = kernel
+        return _spmm_raw(W, X_c)
+
+    @staticmethod
+    def backward(ctx, dY):
+        W_values, X = ctx.saved_tensors
+        W = ctx.W
+        dY_c = dY.to(dtype=torch.float32).contiguous()
+        if dY_c.shape[0] != W.nrows or dY_c.shape[1] != X.shape[1]:
+            raise ValueError(f"spmm_grad_w_simd: dY shape {tuple(dY_c.shape)} does not match "
+                             f"(W.nrows={W.nrows}, N={X.shape[1]})")
+        dW = _sddmm_raw(W, dY_c, X) if ctx.needs_input_grad[0] else None
+        dX = None
+        if ctx.needs_input_grad[2]:
+            WT = _cached_transpose(W)
+            dX = _spmm_raw(WT, dY_c)
+        return dW, None, dX, None
+
+
+def spmm(W: PaddedCSR, X: torch.Tensor, *, kernel: str = "auto") -> torch.Tensor:
+    """Y = W @ X for a PaddedCSR W (M,K) and dense CUDA X (K,N) -> (M,N) fp32.
+
+    Routes through autograd when X or W.values requires grad.
+    Raises TypeError (wrong types), ValueError (ndim / shape / kernel name),
+    RuntimeError (X not on W's CUDA device).
+    """
+    if not isinstance(W, PaddedCSR):
+        raise TypeError(f"spmm: W must be a sparselab.PaddedCSR, got {type(W).__name__}")
+    if not isinstance(X, torch.Tensor):
+        raise TypeError(f"spmm: X must be a torch.Tensor, got {type(X).__name__}")
+    if X.device.type != "cuda":
+        raise RuntimeError(f"spmm: X must be on a CUDA device (got device={X.device}). "
+                           f"sparsecore_b200 has no CPU path.")
+    if X.dim() != 2:
+        raise ValueError(f"spmm: X must be 2-D, got shape={tuple(X.shape)}")
+    if kernel not in _VALID_KERNELS:
+        raise ValueError(f"spmm: unknown kernel={kernel!r}. Expected one of: "
+                         f"{sorted(_VALID_KERNELS)}.")
+    X_f32 = X.to(dtype=torch.float32).contiguous()
+    W_values = W.values
+    if X_f32.requires_grad or W_values.requires_grad:
+        return _SpMMFunction.apply(W_values, W, X_f32, kernel)
+    return _spmm_raw(W, _check_dense(W, X_f32, "spmm_simd"))
