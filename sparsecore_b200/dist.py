@@ -1,0 +1,190 @@
+"""Data-parallel training over NCCL for models with SparseLinear layers.
+
+The reference has no distributed path; this adds the one the benchmark
+needs.  Every rank holds a full replica with the same topology; the batch is
+sharded.  Per step:
+
+* ``allreduce_grads()`` -- ONE collective: the live-slot gradients of every
+  SparseLinear (packed out of the padded ``total_capacity`` layout by
+  ``sl_pack_live``; padding never travels) and all dense gradients are
+  concatenated into one flat fp32 bucket, all-reduced with ReduceOp.AVG and
+  scattered back (``sl_unpack_live``).
+* after a router update, ``broadcast_topology(src=0)`` sends rank 0's
+  ``col_indices`` / ``row_nnz`` / ``values`` of every layer (one flat int32
+  and one flat fp32 broadcast) plus the topology versions, so all replicas
+  hold the same mask even when the grow decision uses rank-local data
+  (RigL's dense gradient).
+* ``topology_checksum()`` all-gathers a per-rank checksum of the masks to
+  detect divergence.
+
+Host-side planning (bucket offsets, which tensors travel) is independent of
+the device kernels; ``pack`` / ``unpack`` can be swapped (tests on CPU gloo
+ranks use index-based stand-ins).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+from . import _native as N
+
+
+@dataclass
+class _Slot:
+    kind: str          # "sparse" | "dense"
+    module: object     # SparseLinear for sparse
+    param: torch.Tensor
+    offset: int
+    length: int
+
+
+def _gpu_pack(layer, offsets: torch.Tensor, src: torch.Tensor, dst: torch.Tensor) -> None:
+    csr = layer._csr
+    N.check(N.lib().sl_pack_live(csr._abi_ref(), N.ptr(offsets), N.ptr(src), N.ptr(dst),
+                                 csr._stream()), "pack_live")
+
+
+def _gpu_unpack(layer, offsets: torch.Tensor, src: torch.Tensor, dst: torch.Tensor) -> None:
+    csr = layer._csr
+    N.check(N.lib().sl_unpack_live(csr._abi_ref(), N.ptr(offsets), N.ptr(src), N.ptr(dst), 1.0,
+                                   csr._stream()), "unpack_live")
+
+
+def _gpu_offsets(layer) -> torch.Tensor:
+    csr = layer._csr
+    out = torch.empty(csr.nrows, dtype=torch.int32, device=csr.device)
+    total = torch.empty(1, dtype=torch.int64, device=csr.device)
+    N.check(N.lib().sl_exclusive_scan(N.ptr(csr.row_nnz), csr.nrows, N.ptr(out), N.ptr(total),
+                                      csr._stream()), "packed offsets")
+    return out
+
+
+class SparseDataParallel:
+    """Gradient / topology synchronisation for a replicated model."""
+
+    def __init__(self, model: torch.nn.Module, process_group=None,
+                 pack: Callable | None = None, unpack: Callable | None = None,
+                 offsets: Callable | None = None, sparse_layers: list | None = None):
+        from .nn import SparseLinear
+
+        self.model = model
+        self.pg = process_group
+        self.sparse_layers = (list(sparse_layers) if sparse_layers is not None else
+                              [m for m in model.modules() if isinstance(m, SparseLinear)])
+        sparse_ids = {id(m._values) for m in self.sparse_layers}
+        self.dense_params = [p for p in model.parameters()
+                             if p.requires_grad and id(p) not in sparse_ids]
+        self._pack = pack or _gpu_pack
+        self._unpack = unpack or _gpu_unpack
+        self._offsets_fn = offsets or _gpu_offsets
+        self._plan_key = None
+        self._plan: list[_Slot] = []
+        self._bucket: torch.Tensor | None = None
+        self._offsets: dict[int, torch.Tensor] = {}
+
+    # ── planning ────────────────────────────────────────────────────────
+    def _key(self):
+        return tuple((m._csr.topology_version, m._csr.nnz) for m in self.sparse_layers)
+
+    def plan(self) -> list[_Slot]:
+        key = self._key()
+        if key == self._plan_key:
+            return self._plan
+        slots, off = [], 0
+        for m in self.sparse_layers:
+            slots.append(_Slot("sparse", m, m._values, off, m._csr.nnz))
+            off += m._csr.nnz
+        for p in self.dense_params:
+            slots.append(_Slot("dense", None, p, off, p.numel()))
+            off += p.numel()
+        dev = slots[0].param.device if slots else torch.device("cpu")
+        if self._bucket is None or self._bucket.numel() != off:
+            self._bucket = torch.empty(off, dtype=torch.float32, device=dev)
+        self._offsets = {id(m): self._offsets_fn(m) for m in self.sparse_layers}
+        self._plan, self._plan_key = slots, key
+        return slots
+
+    @property
+    def bucket_numel(self) -> int:
+        return sum(s.length for s in self.plan())
+
+    # ── per-step gradient exchange ──────────────────────────────────────
+    def allreduce_grads(self) -> None:
+        world = dist.get_world_size(self.pg)
+        if world == 1:
+            return
+        slots = self.plan()
+        buf = self._bucket
+        for s in slots:
+            view = buf[s.offset:s.offset + s.length]
+            g = s.param.grad
+            if s.kind == "sparse":
+                if g is None:
+                    view.zero_()
+                else:
+                    self._pack(s.module, self._offsets[id(s.module)], g, view)
+            else:
+                view.copy_(g.reshape(-1)) if g is not None else view.zero_()
+        if dist.get_backend(self.pg) == "nccl":
+            dist.all_reduce(buf, op=dist.ReduceOp.AVG, group=self.pg)
+        else:
+            dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=self.pg)
+            buf.div_(world)
+        for s in slots:
+            view = buf[s.offset:s.offset + s.length]
+            if s.param.grad is None:
+                s.param.grad = torch.zeros_like(s.param)
+            if s.kind == "sparse":
+                self._unpack(s.module, self._offsets[id(s.module)], view, s.param.grad)
+            else:
+                s.param.grad.copy_(view.view_as(s.param.grad))
+
+    # ── topology synchronisation ────────────────────────────────────────
+    def broadcast_topology(self, src: int = 0) -> None:
+        """Make every replica's masks (and values) equal to rank ``src``'s."""
+        if dist.get_world_size(self.pg) == 1 or not self.sparse_layers:
+            return
+        ints = torch.cat([torch.cat([m._csr.col_indices, m._csr.row_nnz]) for m in self.sparse_layers])
+        flts = torch.cat([m._csr.values for m in self.sparse_layers])
+        vers = torch.tensor([m._csr.topology_version for m in self.sparse_layers],
+                            dtype=torch.int64, device=ints.device)
+        for t in (ints, flts, vers):
+            dist.broadcast(t, src=src, group=self.pg)
+        io = fo = 0
+        for m, v in zip(self.sparse_layers, vers.tolist()):
+            csr = m._csr
+            cap, M = csr.total_capacity, csr.nrows
+            with torch.no_grad():
+                csr.col_indices.copy_(ints[io:io + cap])
+                csr.row_nnz.copy_(ints[io + cap:io + cap + M])
+                csr.values.copy_(flts[fo:fo + cap])
+            io += cap + M
+            fo += cap
+            csr._sync_row_nnz_from_device()
+            csr.topology_version_ = int(v)
+
+    def topology_checksum(self) -> list[int]:
+        """All ranks' mask checksums (equal when the replicas agree)."""
+        h = 0
+        for m in self.sparse_layers:
+            c = m._csr.col_indices.to(torch.int64)
+            idx = torch.arange(c.numel(), device=c.device, dtype=torch.int64)
+            h = (h * 1000003 + int(((c + 7) * (idx % 65521 + 1)).sum().item())) % (2 ** 61 - 1)
+        t = torch.tensor([h], dtype=torch.int64,
+                         device=self.sparse_layers[0]._csr.device if self.sparse_layers else "cpu")
+        out = [torch.zeros_like(t) for _ in range(dist.get_world_size(self.pg))]
+        dist.all_gather(out, t, group=self.pg)
+        return [int(x.item()) for x in out]
+
+
+def sync_after_router_step(ddp: SparseDataParallel, algo, src: int = 0) -> bool:
+    """Broadcast the topology if ``algo.step()`` just ran an update."""
+    if getattr(algo, "last_update_step", None) == getattr(algo, "_step_idx", -1):
+        ddp.broadcast_topology(src)
+        return True
+    return False
+
+

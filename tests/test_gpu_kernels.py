@@ -1,0 +1,159 @@
+"""GPU parity: forward SpMM, SDDMM dW, transpose + dX and dense_grad against
+the reference's golden outputs (bit-exact), through the C-ABI library."""
+import numpy as np
+import pytest
+import torch
+
+from gpu_helpers import bits_equal, csr_from_golden, csr_matches, dev, host, oracle_csr, sha
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("idx", range(12))
+def test_kernels_bit_exact_vs_reference(golden, idx):
+    import sparsecore_b200 as sl
+    from sparsecore_b200 import ops
+
+    p = f"k{idx}_"
+    W = csr_from_golden(golden, p + "W_")
+    X = torch.from_numpy(golden[p + "X"]).to(dev())
+    dY = torch.from_numpy(golden[p + "dY"]).to(dev())
+    assert bits_equal(sl.spmm(W, X), golden[p + "Y"])
+    assert bits_equal(ops._sddmm_raw(W, dY, X), golden[p + "dW"])
+    WT, perm = sl.transpose_with_perm(W)
+    assert csr_matches(WT, golden, p + "WT_")
+    assert np.array_equal(host(perm), golden[p + "perm"])
+    assert bits_equal(ops._spmm_raw(WT, dY), golden[p + "dX"])
+    assert bits_equal(sl.dense_grad(dY, X), golden[p + "G"])
+
+
+@pytest.mark.parametrize("idx", [0, 3, 6, 10])
+def test_autograd_matches_reference(golden, idx):
+    import sparsecore_b200 as sl
+    from sparsecore_b200.ops import _clear_transpose_cache
+
+    _clear_transpose_cache()
+    p = f"k{idx}_"
+    W = csr_from_golden(golden, p + "W_")
+    X = torch.from_numpy(golden[p + "X"]).to(dev()).requires_grad_(True)
+    dY = torch.from_numpy(golden[p + "dY"]).to(dev())
+    Wv = torch.nn.Parameter(W.values)
+    from sparsecore_b200.ops import _SpMMFunction
+
+    Y = _SpMMFunction.apply(Wv, W, X, "simd")
+    Y.backward(dY)
+    assert bits_equal(Y, golden[p + "Y"])
+    assert bits_equal(Wv.grad, golden[p + "dW"])
+    assert bits_equal(X.grad, golden[p + "dX"])
+    # the Parameter aliases the CSR storage
+    assert Wv.data_ptr() == W.values.data_ptr()
+
+
+def test_random_factory_matches_reference(golden):
+    import sparsecore_b200 as sl
+
+    for idx, (M, K, N, s, seed) in enumerate(golden.meta["kernel_cases"]):
+        W = sl.PaddedCSR.random(M, K, sparsity=s, seed=seed)
+        assert csr_matches(W, golden, f"k{idx}_W_"), idx
+
+
+def test_config1_sparse_linear_bit_exact(golden):
+    """cfg1: SparseLinear(784,256,90%) init + Y/dW/dX vs reference hashes."""
+    import sparsecore_b200 as sl
+    from sparsecore_b200 import ops
+
+    m = golden.meta["cfg1"]
+    torch.manual_seed(0)
+    layer = sl.SparseLinear(784, 256, sparsity=0.9, bias=False)
+    W = layer._csr
+    assert W.nnz == m["nnz"] and W.total_capacity == m["total_capacity"]
+    assert sha(host(W.values)) == m["sha_values"]
+    assert sha(host(W.col_indices)) == m["sha_cols"]
+    g = torch.Generator().manual_seed(1)
+    X = torch.randn(784, 256, generator=g)
+    dY = torch.randn(256, 256, generator=g)
+    assert sha(X.numpy()) == m["sha_X"] and sha(dY.numpy()) == m["sha_dY"]
+    X, dY = X.to(dev()), dY.to(dev())
+    assert sha(host(sl.spmm(W, X))) == m["sha_Y"]
+    assert sha(host(ops._sddmm_raw(W, dY, X))) == m["sha_dW"]
+    WT, perm = sl.transpose_with_perm(W)
+    assert sha(host(WT.col_indices)) == m["sha_WT_cols"]
+    assert sha(host(perm)) == m["sha_perm"]
+    assert sha(host(ops._spmm_raw(WT, dY))) == m["sha_dX"]
+
+
+@pytest.mark.parametrize("M,K,N,s", [(4096, 4096, 32, 0.9), (4096, 4096, 256, 0.9),
+                                     (16384, 4096, 1, 0.5), (2048, 4096, 257, 0.99),
+                                     (1024, 3072, 96, 0.9)])
+def test_config3_shapes_vs_oracle(M, K, N, s):
+    """Standalone SpMM sweep shapes: GPU vs the C oracle, bit-exact."""
+    import sparsecore_b200 as sl
+    from oracle import oracle as O
+    from sparsecore_b200 import ops
+
+    g = torch.Generator().manual_seed(M + N)
+    mask = torch.rand(M, K, generator=g) < (1 - s)
+    Wd = torch.randn(M, K, generator=g) * 0.02 * mask
+    W = sl.PaddedCSR.from_dense(Wd.to(dev()))
+    X = torch.randn(K, N, generator=g)
+    dY = torch.randn(M, N, generator=g)
+    Xd, dYd = X.to(dev()), dY.to(dev())
+    Wo = oracle_csr(W)
+    assert bits_equal(sl.spmm(W, Xd), O.spmm(Wo, X.numpy()))
+    assert bits_equal(ops._sddmm_raw(W, dYd, Xd), O.sddmm(Wo, dY.numpy(), X.numpy()))
+    WT, perm = sl.transpose_with_perm(W)
+    WTo, permo = O.transpose_with_perm(Wo)
+    assert np.array_equal(host(WT.col_indices), WTo.cols)
+    assert np.array_equal(host(perm), permo)
+    assert bits_equal(ops._spmm_raw(WT, dYd), O.spmm(WTo, dY.numpy()))
+
+
+def test_edge_cases():
+    import sparsecore_b200 as sl
+    from oracle import oracle as O
+    from sparsecore_b200 import ops
+
+    d = dev()
+    # empty rows, one dense row, N=1 / N=5 (unaligned vectors), unaligned base pointer
+    Wd = torch.zeros(9, 13)
+    Wd[2, 3] = 1.5
+    Wd[4] = torch.arange(13, dtype=torch.float32) - 6
+    Wd[7, 12] = -2.0
+    W = sl.PaddedCSR.from_dense(Wd.to(d))
+    assert W.nnz == 1 + 12 + 1
+    Wo = oracle_csr(W)
+    for N in (1, 2, 5, 16, 17, 31, 64, 129):
+        X = torch.randn(13, N)
+        dY = torch.randn(9, N)
+        assert bits_equal(sl.spmm(W, X.to(d)), O.spmm(Wo, X.numpy()))
+        assert bits_equal(ops._sddmm_raw(W, dY.to(d), X.to(d)), O.sddmm(Wo, dY.numpy(), X.numpy()))
+        # base pointer offset by one float -> not 16-byte aligned
+        buf = torch.empty(13 * N + 1, device=d)
+        Xu = buf[1:].view(13, N)
+        Xu.copy_(X)
+        assert bits_equal(sl.spmm(W, Xu), O.spmm(Wo, X.numpy()))
+    # all-zero matrix, zero-capacity matrix, N = 0
+    Z = sl.PaddedCSR.from_dense(torch.zeros(5, 7, device=d))
+    assert Z.nnz == 0 and Z.total_capacity == 5
+    assert torch.count_nonzero(sl.spmm(Z, torch.randn(7, 3, device=d))) == 0
+    E = sl.PaddedCSR(4, 6)
+    assert E.total_capacity == 0
+    assert torch.count_nonzero(sl.spmm(E, torch.randn(6, 4, device=d))) == 0
+    assert sl.spmm(W, torch.randn(13, 0, device=d)).shape == (9, 0)
+    # transpose of an empty / zero-capacity matrix
+    ET = sl.PaddedCSR.transpose(E)
+    assert ET.shape == (6, 4) and ET.nnz == 0 and ET.total_capacity == 6
+
+
+def test_transpose_involution_and_padding_ratio():
+    import sparsecore_b200 as sl
+
+    W = sl.PaddedCSR.random(300, 200, sparsity=0.9, seed=3)
+    WT = W.transpose()
+    WTT = WT.transpose()
+    assert torch.equal(WTT.to_dense(), W.to_dense())
+    assert torch.equal(WT.to_dense(), W.to_dense().t())
+    W0 = W.transpose(padding_ratio=0.0)
+    assert W0.padding_slots == int((host(W0.row_nnz) == 0).sum())
+    with pytest.raises(ValueError):
+        W.transpose(padding_ratio=-1.0)
