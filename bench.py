@@ -1,0 +1,438 @@
+"""Benchmark: sparse-training tokens/s of the byte-level mini-GPT (config 5)
+on 1..8 B200 (data parallel, one process per GPU), with the SpMM / SDDMM
+roofline of the dominant kernel and the reference's CPU implementation timed
+beside it.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
+
+Prints ONE JSON line (rank 0).  A "step" is one training step of config 5
+on one 32 x 512-token batch per GPU: forward, backward (SDDMM dW + dX on the
+cached transpose), values-only gradient all-reduce across ranks, AdamW, and
+the SET router step (an update fires every 200 steps).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+METRIC = "SpMM fwd+bwd GB/s vs HBM peak; sparse-train tokens/s at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seqs", type=int, default=2, help="sequences per CPU sample step")
+    ap.add_argument("--kernel", default=None,
+                    help="profiling mode: SHAPE:KIND:N runs 2 launches of one kernel "
+                         "(SHAPE in %s or MxK@sparsity; KIND fwd|dw|dx|transpose)" % list(SHAPES))
+    ap.add_argument("--sweep", action="store_true",
+                    help="config-3 standalone SpMM sweep: one JSON line per cell")
+    return ap.parse_args()
+
+
+# Layer shapes of the configs: (M out, K in, sparsity).
+SHAPES = {"ffn_up": (3072, 768, 0.9), "ffn_down": (768, 3072, 0.9), "qkv": (2304, 768, 0.7),
+          "o": (768, 768, 0.7), "cfg1": (256, 784, 0.9)}
+
+
+def _shape(spec):
+    if spec in SHAPES:
+        return SHAPES[spec]
+    mk, sp = spec.split("@")
+    m, k = mk.lower().split("x")
+    return int(m), int(k), float(sp)
+
+
+def _sweep_matrix(M, K, s, seed=0):
+    import sparsecore_b200 as sl
+
+    g = torch.Generator().manual_seed(seed)
+    mask = torch.rand(M, K, generator=g) < (1 - s)
+    Wd = (torch.randn(M, K, generator=g) * 0.02) * mask
+    return sl.PaddedCSR.from_dense(Wd.cuda())
+
+
+def run_kernel_case(spec):
+    """Two launches of one kernel on synthetic inputs (for ncu captures)."""
+    import sparsecore_b200 as sl
+    from sparsecore_b200 import ops
+
+    name, kind, n = spec.split(":")
+    M, K, s = _shape(name)
+    N = int(n)
+    W = _sweep_matrix(M, K, s)
+    X = torch.randn(K, N, device="cuda")
+    dY = torch.randn(M, N, device="cuda")
+    WT, _ = sl.transpose_with_perm(W)
+    for _ in range(2):
+        if kind == "fwd":
+            ops._spmm_raw(W, X)
+        elif kind == "dw":
+            ops._sddmm_raw(W, dY, X)
+        elif kind == "dx":
+            ops._spmm_raw(WT, dY)
+        else:
+            sl.transpose_with_perm(W)
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel_case": spec, "M": M, "K": K, "N": N, "nnz": W.nnz}))
+
+
+def run_sweep(args):
+    """Config 3: W in {4096x4096, 16384x4096} x sparsity x N; fwd, SDDMM, dX."""
+    import sparsecore_b200 as sl
+    from sparsecore_b200 import ops
+
+    hbm, src, sm_max = peaks()
+    fp32 = 148 * 128 * 2 * sm_max * 1e6 / 1e12
+
+    def t_ms(fn, it=10):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(it):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        return sorted(ts)[len(ts) // 2]
+
+    for (M, K) in [(4096, 4096), (16384, 4096)]:
+        for s in (0.5, 0.8, 0.9, 0.95, 0.99):
+            W = _sweep_matrix(M, K, s)
+            WT, _ = sl.transpose_with_perm(W)
+            nnz = W.nnz
+            for N in (1, 32, 256, 2048, 8192):
+                if 4 * (K * N + M * N) * 3 > 60e9:
+                    continue
+                X = torch.randn(K, N, device="cuda")
+                dY = torch.randn(M, N, device="cuda")
+                cell = {"M": M, "K": K, "sparsity": s, "N": N, "nnz": nnz}
+                for kind, fn, byt in (
+                        ("fwd", lambda: ops._spmm_raw(W, X), 8 * nnz + 8 * M + 4 * K * N + 4 * M * N),
+                        ("dw", lambda: ops._sddmm_raw(W, dY, X), 8 * nnz + 8 * M + 4 * M * N + 4 * K * N),
+                        ("dx", lambda: ops._spmm_raw(WT, dY), 8 * nnz + 8 * K + 4 * M * N + 4 * K * N)):
+                    ms = t_ms(fn)
+                    gbs = byt / (ms * 1e-3) / 1e9
+                    tfl = 2 * nnz * N / (ms * 1e-3) / 1e12
+                    hbm_floor = byt / (hbm * 1e9) * 1e3
+                    fma_floor = 2 * nnz * N / (fp32 * 1e12) * 1e3
+                    cell[kind] = {"ms": round(ms, 4), "GB/s": round(gbs, 1),
+                                  "hbm_frac": round(gbs / hbm, 3), "TFLOP/s": round(tfl, 2),
+                                  "fp32_frac": round(tfl / fp32, 3),
+                                  "bound": "hbm" if hbm_floor >= fma_floor else "fp32-fma",
+                                  "binding_frac": round(max(hbm_floor, fma_floor) / ms, 3)}
+                print(json.dumps(cell), flush=True)
+                del X, dY
+            del W, WT
+            torch.cuda.empty_cache()
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured", float(p.get("sm_max_mhz", 1965.0))
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback", 1965.0
+
+
+def workload_config(cfg, world):
+    return {
+        "workload": (f"{cfg.name}: d_model {cfg.d_model}, {cfg.n_layers} layers, {cfg.n_heads} "
+                     f"heads, ctx {cfg.seq_len}, vocab {cfg.vocab}, FFN {cfg.d_ff} at "
+                     f"{int(cfg.ffn_sparsity * 100)}% / attention projections at "
+                     f"{int(cfg.attn_sparsity * 100)}% sparsity (padded CSR, fp32), AdamW "
+                     f"{cfg.lr}, {cfg.router} every {cfg.update_freq} steps"),
+        "global_batch": cfg.batch * world,
+        "seq_len": cfg.seq_len,
+        "tokens_per_step": cfg.batch * cfg.seq_len * world,
+        "parallelism": f"dp{world}",
+        "l2": "inputs larger than L2 (per-step activations ~GBs, no flush needed)",
+    }
+
+
+# ───────────────────────────── clocks ─────────────────────────────
+
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms",
+                 "200", "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.p.terminate()
+        out, _ = self.p.communicate(timeout=10)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ───────────────────────────── our arm ─────────────────────────────
+
+def run_ours(args, rank, world, local_rank):
+    import sparsecore_b200 as sl
+    from sparsecore_b200 import _native as N
+    from sparsecore_b200 import ops
+    from sparsecore_b200.dist import SparseDataParallel, sync_after_router_step
+    from sparsecore_b200.workloads import CFG5, MiniGPT, lm_loss, sparse_live_weights, synthetic_tokens
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    cfg = CFG5
+    torch.manual_seed(0)  # identical replicas on every rank
+    model = MiniGPT(cfg, device=dev)
+    algo = sl.SET(sparsity=cfg.ffn_sparsity, drop_fraction=cfg.drop_fraction,
+                  update_freq=cfg.update_freq, seed=0)
+    model.apply(algo)
+    opt = torch.optim.AdamW(model.parameters(), lr=cfg.lr)
+    ddp = SparseDataParallel(model)
+    tokens_host = synthetic_tokens(cfg, cfg.batch, seed=1000 + rank).pin_memory()
+    tokens_dev = tokens_host.to(dev)
+
+    def step(tok):
+        opt.zero_grad(set_to_none=True)
+        loss = lm_loss(model, tok)
+        loss.backward()
+        ddp.allreduce_grads()
+        opt.step()
+        algo.step()
+        sync_after_router_step(ddp, algo)
+        return loss
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step(tokens_dev)
+    barrier()
+
+    timer = ops.KernelTimer()
+    ops.set_kernel_timer(timer)
+    clocks = Clocks(local_rank)
+    clocks.start()
+    l0 = N.launches["count"]
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(s)
+    for _ in range(args.steps):
+        step(tokens_dev)
+    e1.record(s)
+    barrier()
+    launches = N.launches["count"] - l0
+    clk = clocks.stop()
+    ops.set_kernel_timer(None)
+    t_ms = e0.elapsed_time(e1)
+    ksum = timer.summary()
+
+    # end to end: host tokens (pinned) -> device every step, loss read back
+    barrier()
+    w0 = time.perf_counter()
+    for _ in range(args.steps):
+        tok = tokens_host.to(dev, non_blocking=True)
+        float(step(tok).item())
+    barrier()
+    e2e_ms = (time.perf_counter() - w0) * 1e3
+
+    # one router update + topology broadcast, timed on its own
+    barrier()
+    r0 = time.perf_counter()
+    algo.update()
+    ddp.broadcast_topology(0)
+    barrier()
+    router_ms = (time.perf_counter() - r0) * 1e3
+
+    t = torch.tensor([t_ms, e2e_ms, router_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t_ms, e2e_ms, router_ms = t.tolist()
+    if rank != 0:
+        return None
+
+    tokens = cfg.batch * cfg.seq_len * world * args.steps
+    hbm, hbm_src, sm_max = peaks()
+    dom = max(ksum, key=lambda k: ksum[k]["ms"]) if ksum else None
+    roof = None
+    if dom:
+        d = ksum[dom]
+        gbs = d["bytes"] / (d["ms"] * 1e-3) / 1e9
+        tfl = d["flops"] / (d["ms"] * 1e-3) / 1e12
+        fp32_peak = 148 * 128 * 2 * sm_max * 1e6 / 1e12
+        roof = {"bound": "hbm", "kernel": dom, "achieved": round(gbs, 1), "peak": hbm,
+                "unit": "GB/s", "frac": round(gbs / hbm, 4), "peak_source": f"{hbm_src} (MEASURED_PEAKS.json hbm_gbs)",
+                "traffic": read_traffic(dom), "launches": d["launches"],
+                "avg_launch_ms": round(d["ms"] / d["launches"], 4),
+                "achieved_fp32_tflops": round(tfl, 2),
+                "fp32_fma_peak_tflops": round(fp32_peak, 1),
+                "fp32_frac": round(tfl / fp32_peak, 4),
+                "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 2),
+                                "GB/s": round(v["bytes"] / (v["ms"] * 1e-3) / 1e9, 1),
+                                "TFLOP/s": round(v["flops"] / (v["ms"] * 1e-3) / 1e12, 2)}
+                            for k, v in ksum.items()},
+                "step_share": round(sum(v["ms"] for v in ksum.values()) / t_ms, 3)}
+    line = {
+        "metric": METRIC, "value": round(tokens / (t_ms * 1e-3), 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(t_ms / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (uniform random byte tokens)",
+        "config": dict(workload_config(cfg, world), sparse_live_weights=sparse_live_weights(model)),
+        "roofline": roof,
+        "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": tokens_host.numel() * tokens_host.element_size(),
+                "d2h_bytes_per_step": 4},
+        "gpu_launches": launches,
+        "clocks": clk,
+        "router": {"algorithm": "SET", "every_steps": cfg.update_freq,
+                   "update_plus_broadcast_ms": round(router_ms, 1),
+                   "note": "no update falls inside the timed window; amortised cost per step = "
+                           "update_plus_broadcast_ms / every_steps"},
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_sample(cfg, args.cpu_seqs, 1, 2)
+    return line
+
+
+def read_traffic(kernel):
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summary, if any."""
+    path = os.path.join(REPO, "profiles", "ncu_traffic.txt")
+    try:
+        for line in open(path):
+            f = line.split()
+            if len(f) >= 2 and f[0] == kernel:
+                return float(f[1])
+    except OSError:
+        pass
+    return None
+
+
+# ───────────────────────────── reference arm ─────────────────────────────
+
+def cpu_sample(cfg, seqs, warmup, steps):
+    """The reference's CPU implementation of the path on a bounded sample."""
+    threads = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    torch.set_num_threads(threads)
+    from oracle import ref_arm
+    from sparsecore_b200.workloads import MiniGPT, lm_loss, synthetic_tokens
+
+    kern = ref_arm.kernels()
+    torch.manual_seed(0)
+    model = MiniGPT(cfg, device="cpu", linear=ref_arm.linear_factory(kern))
+    opt = torch.optim.AdamW(model.parameters(), lr=cfg.lr)
+    tok = synthetic_tokens(cfg, seqs, seed=1000)
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        loss = lm_loss(model, tok)
+        loss.backward()
+        opt.step()
+        return float(loss.item())
+
+    for _ in range(warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = time.perf_counter() - t0
+    return {"value": round(seqs * cfg.seq_len * steps / dt, 2), "unit": "tokens/s",
+            "cores": threads if kern.kind == "reference" else 1, "kind": kern.kind,
+            "sample": f"{steps} training steps of {seqs} x {cfg.seq_len} tokens (config-5 model, "
+                      f"{warmup} warm-up), reference _core kernels (OpenMP) + torch CPU dense ops",
+            "ms_per_step": round(dt / steps * 1e3, 1)}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    from sparsecore_b200.workloads import CFG5
+
+    cfg = CFG5
+    cb = cpu_sample(cfg, args.cpu_seqs, max(1, min(args.warmup, 2)), max(1, min(args.steps, 5)))
+    return {
+        "metric": METRIC, "impl": "reference", "value": cb["value"], "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": cb["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (uniform random byte tokens)",
+        "config": workload_config(cfg, world), "cpu_baseline": cb,
+        "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if REPO not in sys.path:
+        sys.path.insert(0, REPO)
+    if args.kernel:
+        run_kernel_case(args.kernel)
+        return
+    if args.sweep:
+        run_sweep(args)
+        return
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+    else:
+        if world > 1:
+            torch.cuda.set_device(local_rank)
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+        line = run_ours(args, rank, world, local_rank)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -56,6 +56,10 @@ typedef struct sl_csr {
 SL_API const char* sl_last_error(void);
 /* Library version string. */
 SL_API const char* sl_version(void);
+/* Status word of the current device (synchronous): bit 0 set = a bounded
+ * device-side wait (TMA / mbarrier) gave up instead of hanging; that call's
+ * output is invalid.  reset != 0 clears the word after reading. */
+SL_API int sl_device_status(int reset, unsigned* out);
 
 /* ── Forward SpMM ─────────────────────────────────────────────────────────
  * Y[M,N] = W[M,K] . X[K,N].  Each Y element is the fp32 FMA chain over the

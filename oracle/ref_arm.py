@@ -1,0 +1,151 @@
+"""CPU reference arm: the reference's own compiled kernels on the host cores.
+
+TEST / MEASUREMENT INFRASTRUCTURE ONLY (used by bench.py's reference arm and
+cpu_baseline leg).  The sparse projections call the reference's ``_core``
+extension -- compiled from the reference sources by oracle/Makefile into
+oracle/_ref/refcore/ -- exactly as the reference's ``_SpMMFunction`` does
+(sparselab/ops.py:145-210): forward ``spmm_simd(W, X)``, backward
+``spmm_grad_w_simd(W, dY, X)`` and ``spmm_simd(W^T, dY)`` over a transpose
+cached per topology and value-refreshed through its permutation
+(sparselab/ops.py:70-99).  Everything else (embeddings, LayerNorm, attention,
+AdamW) is stock torch on the CPU, as in the reference's demos.
+
+If the reference ``_core`` was not built, the kernels fall back to the C
+oracle (single-threaded restatement) and the arm reports kind "port".
+"""
+from __future__ import annotations
+
+import importlib.util
+import math
+import os
+
+import numpy as np
+import torch
+import torch.nn as nn
+
+from . import oracle as O
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_core = None
+
+
+def load_refcore():
+    """The reference's compiled `_core` module, or None if not built."""
+    global _core
+    if _core is not None:
+        return _core
+    d = os.path.join(_HERE, "_ref", "refcore")
+    if not os.path.isdir(d):
+        return None
+    for f in os.listdir(d):
+        if f.startswith("_core") and f.endswith(".so"):
+            spec = importlib.util.spec_from_file_location("_core", os.path.join(d, f))
+            mod = importlib.util.module_from_spec(spec)
+            spec.loader.exec_module(mod)
+            _core = mod
+            return mod
+    return None
+
+
+class _RefSpMM(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, W_values, layer, X):
+        ctx.layer = layer
+        ctx.save_for_backward(X)
+        return torch.from_numpy(layer.kernels.fwd(layer.W, X.contiguous().numpy()))
+
+    @staticmethod
+    def backward(ctx, dY):
+        (X,) = ctx.saved_tensors
+        layer = ctx.layer
+        dYn = dY.to(torch.float32).contiguous().numpy()
+        dW = torch.from_numpy(layer.kernels.dw(layer.W, dYn, X.numpy()))
+        WT = layer.cached_transpose()
+        dX = torch.from_numpy(layer.kernels.fwd(WT, dYn))
+        return dW, None, dX
+
+
+class _CoreKernels:
+    kind = "reference"
+
+    def __init__(self, core):
+        self.core = core
+
+    def make(self, p: O.CSR):
+        return self.core.PaddedCSR(p.nrows, p.ncols, p.values.tolist(), p.cols.tolist(),
+                                   p.row_start.tolist(), p.row_nnz.tolist(),
+                                   p.row_capacity.tolist())
+
+    def values(self, W):
+        return np.asarray(W.values)
+
+    def fwd(self, W, X):
+        return self.core.spmm_simd(W, X)
+
+    def dw(self, W, dY, X):
+        return self.core.spmm_grad_w_simd(W, dY, X)
+
+
+class _PortKernels:
+    kind = "port"
+
+    def make(self, p: O.CSR):
+        return p
+
+    def values(self, W):
+        return W.values
+
+    def fwd(self, W, X):
+        return O.spmm(W, X)
+
+    def dw(self, W, dY, X):
+        return O.sddmm(W, dY, X)
+
+
+def kernels():
+    core = load_refcore()
+    return _CoreKernels(core) if core is not None else _PortKernels()
+
+
+class RefSparseLinear(nn.Module):
+    """CPU SparseLinear over the reference kernels; same init draws as the
+    reference (sparselab/nn.py:118-185)."""
+
+    def __init__(self, fin, fout, sparsity, kern, bias=False, padding_ratio=0.2):
+        super().__init__()
+        self.in_features, self.out_features = fin, fout
+        self.kernels = kern
+        fan = max(1.0, fin * (1.0 - sparsity))
+        bound = 1.0 / math.sqrt(fan)
+        Wd = torch.empty(fout, fin)
+        nn.init.uniform_(Wd, -bound, bound)
+        mask = torch.rand(fout, fin) >= sparsity
+        p = O.from_dense((Wd * mask.float()).numpy(), padding_ratio=padding_ratio)
+        self._p = p
+        self.W = kern.make(p)
+        self._values = nn.Parameter(torch.from_numpy(kern.values(self.W)))
+        self.bias = None
+        self._wt = None
+
+    def cached_transpose(self):
+        if self._wt is None:
+            # Topology is fixed inside a timed sample: build W^T once.
+            pT, perm = O.transpose_with_perm(self._p)
+            self._wt = (self.kernels.make(pT), perm, perm >= 0)
+        WT, perm, live = self._wt
+        wt_vals = self.kernels.values(WT)
+        w_vals = self.kernels.values(self.W)
+        wt_vals[live] = w_vals[perm[live]]
+        return WT
+
+    def forward(self, x):
+        shp = x.shape
+        X_col = x.reshape(-1, self.in_features).t().contiguous()
+        y = _RefSpMM.apply(self._values, self, X_col).t()
+        return y.reshape(shp[:-1] + (self.out_features,))
+
+
+def linear_factory(kern):
+    def make(fin, fout, sparsity):
+        return RefSparseLinear(fin, fout, sparsity, kern)
+    return make

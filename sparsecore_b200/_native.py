@@ -43,6 +43,7 @@ class SlCsr(ctypes.Structure):
 SIGNATURES: dict[str, tuple] = {
     "sl_last_error": (ctypes.c_char_p, []),
     "sl_version": (ctypes.c_char_p, []),
+    "sl_device_status": (I32, [I32, P]),
     "sl_spmm_fwd": (I32, [P, P, I64, I64, P, P]),
     "sl_sddmm_dw": (I32, [P, P, P, I64, P, P]),
     "sl_transpose_scratch_bytes": (I64, [I64, I64]),
@@ -115,6 +116,24 @@ def stream_ptr(device: torch.device) -> P:
 
 def ptr(t: torch.Tensor | None) -> P:
     return P(t.data_ptr()) if t is not None else P(0)
+
+
+# Kernels each entry point launches (for launch accounting).
+KERNELS_PER_CALL = {
+    "sl_spmm_fwd": 1, "sl_sddmm_dw": 1, "sl_transpose_count": 3, "sl_transpose_fill": 2,
+    "sl_values_gather": 1, "sl_dense_count": 2, "sl_dense_fill": 1, "sl_capacity_scan": 1,
+    "sl_to_dense": 1, "sl_check_invariants": 2, "sl_dense_grad": 1, "sl_dst_threshold": 9,
+    "sl_dst_keep": 1, "sl_dst_apply_random": 1, "sl_dst_apply_topk": 1, "sl_dst_apply_cols": 1,
+    "sl_pack_live": 1, "sl_unpack_live": 1, "sl_exclusive_scan": 1,
+}
+launches = {"count": 0}
+
+
+def call(name: str, *args) -> None:
+    """Invoke a status-returning entry point; raise on error; count launches."""
+    rc = getattr(lib(), name)(*args)
+    launches["count"] += KERNELS_PER_CALL.get(name, 1)
+    check(rc, name)
 
 
 def check(rc: int, fn: str = "") -> None:

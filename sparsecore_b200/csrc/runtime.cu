@@ -3,7 +3,10 @@
 #include <mutex>
 #include <vector>
 
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace slb {
 
@@ -122,6 +125,45 @@ unpack_live_kernel(int M, const int32_t* __restrict__ row_start,
     }
 }
 
+bool make_tmap_2d(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int box_rows,
+                  int box_cols) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    if (encode == nullptr || !aligned16(base) || (cols * 4) % 16 != 0) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * sizeof(float)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+unsigned* device_status_word() {
+    static std::mutex mu;
+    static std::vector<unsigned*> words;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= static_cast<int>(words.size())) words.resize(dev + 1, nullptr);
+    if (words[dev] == nullptr) {
+        void* p = nullptr;
+        if (cudaMalloc(&p, sizeof(unsigned)) != cudaSuccess) return nullptr;
+        cudaMemset(p, 0, sizeof(unsigned));
+        words[dev] = static_cast<unsigned*>(p);
+    }
+    return words[dev];
+}
+
 int row_grid(int64_t M) {
     const int64_t want = (M + 7) / 8;
     const int64_t cap = static_cast<int64_t>(num_sms()) * 16;
@@ -137,6 +179,19 @@ extern "C" {
 const char* sl_last_error(void) { return slb::g_last_error.c_str(); }
 
 const char* sl_version(void) { return "sparsecore_b200 0.1.0 (sm_100a)"; }
+
+int sl_device_status(int reset, unsigned* out) {
+    unsigned* w = device_status_word();
+    if (w == nullptr) return fail(SL_ERR_CUDA, "sl_device_status: no device status word");
+    unsigned v = 0;
+    if (int rc = cuda_status(cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost),
+                             "sl_device_status"))
+        return rc;
+    if (reset && v)
+        if (int rc = cuda_status(cudaMemset(w, 0, sizeof(unsigned)), "sl_device_status")) return rc;
+    if (out) *out = v;
+    return SL_OK;
+}
 
 int sl_exclusive_scan(const int32_t* counts, int64_t n, int32_t* out, int64_t* total_dev,
                       void* stream) {

@@ -92,7 +92,8 @@ sddmm_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
                 const int64_t j = m * 16 + q * 4;
                 const float4 d = load4<VEC4>(dyr + j);
 #pragma unroll
-                for (int u = 0; u < S; ++u) fma4(d, load4<VEC4>(xr[u] + j), acc[u]);
+                for (int u = 0; u < S; ++u)
+                    if (act[u]) fma4(d, load4<VEC4>(xr[u] + j), acc[u]);
             }
             // acc = acc_a + acc_b (lanes 0,1 receive lanes 2,3).
 #pragma unroll

@@ -43,22 +43,22 @@ class _Slot:
 
 def _gpu_pack(layer, offsets: torch.Tensor, src: torch.Tensor, dst: torch.Tensor) -> None:
     csr = layer._csr
-    N.check(N.lib().sl_pack_live(csr._abi_ref(), N.ptr(offsets), N.ptr(src), N.ptr(dst),
-                                 csr._stream()), "pack_live")
+    N.call("sl_pack_live", csr._abi_ref(), N.ptr(offsets), N.ptr(src), N.ptr(dst),
+                                 csr._stream())
 
 
 def _gpu_unpack(layer, offsets: torch.Tensor, src: torch.Tensor, dst: torch.Tensor) -> None:
     csr = layer._csr
-    N.check(N.lib().sl_unpack_live(csr._abi_ref(), N.ptr(offsets), N.ptr(src), N.ptr(dst), 1.0,
-                                   csr._stream()), "unpack_live")
+    N.call("sl_unpack_live", csr._abi_ref(), N.ptr(offsets), N.ptr(src), N.ptr(dst), 1.0,
+                                   csr._stream())
 
 
 def _gpu_offsets(layer) -> torch.Tensor:
     csr = layer._csr
     out = torch.empty(csr.nrows, dtype=torch.int32, device=csr.device)
     total = torch.empty(1, dtype=torch.int64, device=csr.device)
-    N.check(N.lib().sl_exclusive_scan(N.ptr(csr.row_nnz), csr.nrows, N.ptr(out), N.ptr(total),
-                                      csr._stream()), "packed offsets")
+    N.call("sl_exclusive_scan", N.ptr(csr.row_nnz), csr.nrows, N.ptr(out), N.ptr(total),
+                                      csr._stream())
     return out
 
 
@@ -112,8 +112,11 @@ class SparseDataParallel:
         return sum(s.length for s in self.plan())
 
     # ── per-step gradient exchange ──────────────────────────────────────
+    def world_size(self) -> int:
+        return dist.get_world_size(self.pg) if dist.is_available() and dist.is_initialized() else 1
+
     def allreduce_grads(self) -> None:
-        world = dist.get_world_size(self.pg)
+        world = self.world_size()
         if world == 1:
             return
         slots = self.plan()
@@ -145,7 +148,7 @@ class SparseDataParallel:
     # ── topology synchronisation ────────────────────────────────────────
     def broadcast_topology(self, src: int = 0) -> None:
         """Make every replica's masks (and values) equal to rank ``src``'s."""
-        if dist.get_world_size(self.pg) == 1 or not self.sparse_layers:
+        if self.world_size() == 1 or not self.sparse_layers:
             return
         ints = torch.cat([torch.cat([m._csr.col_indices, m._csr.row_nnz]) for m in self.sparse_layers])
         flts = torch.cat([m._csr.values for m in self.sparse_layers])
@@ -175,7 +178,9 @@ class SparseDataParallel:
             h = (h * 1000003 + int(((c + 7) * (idx % 65521 + 1)).sum().item())) % (2 ** 61 - 1)
         t = torch.tensor([h], dtype=torch.int64,
                          device=self.sparse_layers[0]._csr.device if self.sparse_layers else "cpu")
-        out = [torch.zeros_like(t) for _ in range(dist.get_world_size(self.pg))]
+        if self.world_size() == 1:
+            return [int(t.item())]
+        out = [torch.zeros_like(t) for _ in range(self.world_size())]
         dist.all_gather(out, t, group=self.pg)
         return [int(x.item()) for x in out]
 

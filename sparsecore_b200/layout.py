@@ -201,8 +201,7 @@ class PaddedCSR:
             return (f"Invariant 2 violated: values.size()={nv} does not match "
                     f"total_capacity={total} (sum of row_capacity).")
         rep = torch.empty(4, dtype=torch.int64, device=self._device)
-        N.check(N.lib().sl_check_invariants(self._abi_ref(), nv, N.ptr(rep), self._stream()),
-                "check_invariants")
+        N.call("sl_check_invariants", self._abi_ref(), nv, N.ptr(rep), self._stream())
         code, row, slot, _ = (int(v) for v in rep.cpu().tolist())
         if code == 0:
             return ""
@@ -322,13 +321,13 @@ def from_dense(W: torch.Tensor, *, threshold: float = 0.0, padding_ratio: float 
     M, K = D.shape
     row_nnz, row_cap, row_start, total = _alloc_rows(M, dev)
     s = N.stream_ptr(dev)
-    N.check(N.lib().sl_dense_count(N.ptr(D), M, K, float(threshold), opp, N.ptr(row_nnz),
-                                   N.ptr(row_cap), N.ptr(row_start), N.ptr(total), s), "from_dense")
+    N.call("sl_dense_count", N.ptr(D), M, K, float(threshold), opp, N.ptr(row_nnz),
+                                   N.ptr(row_cap), N.ptr(row_start), N.ptr(total), s)
     cap = int(total.item())
     vals = torch.empty(cap, dtype=torch.float32, device=dev)
     cols = torch.empty(cap, dtype=torch.int32, device=dev)
     out = PaddedCSR._from_device(M, K, vals, cols, row_start, row_nnz, row_cap, dev)
-    N.check(N.lib().sl_dense_fill(N.ptr(D), float(threshold), out._abi_ref(), s), "from_dense")
+    N.call("sl_dense_fill", N.ptr(D), float(threshold), out._abi_ref(), s)
     return out
 
 
@@ -348,8 +347,8 @@ def from_torch_sparse_csr(csr: torch.Tensor, *, padding_ratio: float = 0.2,
     tval = csr.values().to(device=dev, dtype=torch.float32).contiguous()
     row_nnz = (crow[1:] - crow[:-1]).to(torch.int32).contiguous()
     _, row_cap, row_start, total = _alloc_rows(M, dev)
-    N.check(N.lib().sl_capacity_scan(N.ptr(row_nnz), M, opp, N.ptr(row_cap), N.ptr(row_start),
-                                     N.ptr(total), N.stream_ptr(dev)), "from_torch_sparse_csr")
+    N.call("sl_capacity_scan", N.ptr(row_nnz), M, opp, N.ptr(row_cap), N.ptr(row_start),
+                                     N.ptr(total), N.stream_ptr(dev))
     cap = int(total.item())
     vals = torch.zeros(cap, dtype=torch.float32, device=dev)
     cols = torch.full((cap,), -1, dtype=torch.int32, device=dev)
@@ -385,7 +384,7 @@ def random(nrows: int, ncols: int, *, sparsity: float, padding_ratio: float = 0.
 def to_dense(p: PaddedCSR) -> torch.Tensor:
     """PaddedCSR -> dense float32 CUDA tensor (sparselab/layout.py:262-292)."""
     out = torch.empty(p.nrows, p.ncols, dtype=torch.float32, device=p.device)
-    N.check(N.lib().sl_to_dense(p._abi_ref(), N.ptr(out), p._stream()), "to_dense")
+    N.call("sl_to_dense", p._abi_ref(), N.ptr(out), p._stream())
     return out
 
 
@@ -399,15 +398,14 @@ def transpose_with_perm(p: PaddedCSR, *, padding_ratio: float = 0.2):
     s = p._stream()
     row_nnz, row_cap, row_start, total = _alloc_rows(K, dev)
     scratch = torch.empty(int(lib.sl_transpose_scratch_bytes(M, K)), dtype=torch.uint8, device=dev)
-    N.check(lib.sl_transpose_count(p._abi_ref(), opp, N.ptr(row_nnz), N.ptr(row_cap),
-                                   N.ptr(row_start), N.ptr(total), N.ptr(scratch), s), "transpose")
+    N.call("sl_transpose_count", p._abi_ref(), opp, N.ptr(row_nnz), N.ptr(row_cap),
+                                   N.ptr(row_start), N.ptr(total), N.ptr(scratch), s)
     capT = int(total.item())
     vals = torch.empty(capT, dtype=torch.float32, device=dev)
     cols = torch.empty(capT, dtype=torch.int32, device=dev)
     perm = torch.empty(capT, dtype=torch.int64, device=dev)
     WT = PaddedCSR._from_device(K, M, vals, cols, row_start, row_nnz, row_cap, dev)
-    N.check(lib.sl_transpose_fill(p._abi_ref(), WT._abi_ref(), N.ptr(perm), N.ptr(scratch), s),
-            "transpose")
+    N.call("sl_transpose_fill", p._abi_ref(), WT._abi_ref(), N.ptr(perm), N.ptr(scratch), s)
     return WT, perm
 
 

@@ -45,8 +45,8 @@ def _cached_transpose(W: PaddedCSR) -> PaddedCSR:
         WT, perm = hit[2], hit[3]
         n = int(perm.numel())
         if n:
-            N.check(N.lib().sl_values_gather(N.ptr(perm), N.ptr(W.values), N.ptr(WT.values), n,
-                                             W._stream()), "_cached_transpose")
+            N.call("sl_values_gather", N.ptr(perm), N.ptr(W.values), N.ptr(WT.values), n,
+                                             W._stream())
         return WT
     WT, perm = transpose_with_perm(W)
     if hit is None:
@@ -61,21 +61,66 @@ def _clear_transpose_cache() -> None:
     _transpose_cache.clear()
 
 
-def _spmm_raw(W: PaddedCSR, X: torch.Tensor) -> torch.Tensor:
+class KernelTimer:
+    """Optional CUDA-event timing of every SpMM / SDDMM launch (on the stream
+    the kernel is launched on), with the algorithmic bytes and FLOPs of each
+    launch.  Bytes count values+indices once, the gathered dense operand once
+    (K*N), the dense row operand and the output once."""
+
+    def __init__(self):
+        self.records: list[tuple] = []  # (kind, start_event, end_event, bytes, flops)
+
+    def summary(self) -> dict:
+        out: dict = {}
+        for kind, e0, e1, b, f in self.records:
+            d = out.setdefault(kind, {"launches": 0, "ms": 0.0, "bytes": 0, "flops": 0})
+            d["launches"] += 1
+            d["ms"] += e0.elapsed_time(e1)
+            d["bytes"] += b
+            d["flops"] += f
+        return out
+
+
+_timer: KernelTimer | None = None
+
+
+def set_kernel_timer(t: KernelTimer | None) -> None:
+    global _timer
+    _timer = t
+
+
+def _launch(kind, nbytes, flops, fn):
+    if _timer is None:
+        fn()
+        return
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    fn()
+    e1.record(s)
+    _timer.records.append((kind, e0, e1, nbytes, flops))
+
+
+def _spmm_raw(W: PaddedCSR, X: torch.Tensor, kind: str = "spmm_fwd") -> torch.Tensor:
     """Y = W.X on the CUDA kernel; X float32 contiguous on W's device."""
     M = W.nrows
     K, Ncol = X.shape
     Y = torch.empty(M, Ncol, dtype=torch.float32, device=X.device)
-    N.check(N.lib().sl_spmm_fwd(W._abi_ref(), N.ptr(X), K, Ncol, N.ptr(Y), W._stream()),
-            "spmm_simd")
+    nnz = W.nnz
+    _launch(kind, 8 * nnz + 8 * M + 4 * K * Ncol + 4 * M * Ncol, 2 * nnz * Ncol,
+            lambda: N.call("sl_spmm_fwd", W._abi_ref(), N.ptr(X), K, Ncol, N.ptr(Y), W._stream()))
     return Y
 
 
 def _sddmm_raw(W: PaddedCSR, dY: torch.Tensor, X: torch.Tensor) -> torch.Tensor:
     """dW[total_capacity] at live slots (padding 0)."""
     dW = torch.empty(W.total_capacity, dtype=torch.float32, device=dY.device)
-    N.check(N.lib().sl_sddmm_dw(W._abi_ref(), N.ptr(dY), N.ptr(X), dY.shape[1], N.ptr(dW),
-                                W._stream()), "spmm_grad_w_simd")
+    M, Ncol = dY.shape
+    K = X.shape[0]
+    nnz = W.nnz
+    _launch("sddmm_dw", 8 * nnz + 8 * M + 4 * M * Ncol + 4 * K * Ncol, 2 * nnz * Ncol,
+            lambda: N.call("sl_sddmm_dw", W._abi_ref(), N.ptr(dY), N.ptr(X), Ncol, N.ptr(dW),
+                           W._stream()))
     return dW
 
 
@@ -121,7 +166,7 @@ class _SpMMFunction(torch.autograd.Function):
         dX = None
         if ctx.needs_input_grad[2]:
             WT = _cached_transpose(W)
-            dX = _spmm_raw(WT, dY_c)
+            dX = _spmm_raw(WT, dY_c, kind="spmm_dx")
         return dW, None, dX, None
 
 

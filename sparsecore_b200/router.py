@@ -126,12 +126,11 @@ class _Prune:
         self.k_drop = max(1, int(drop_fraction * total))
         self.thr = torch.empty(1, dtype=torch.float32, device=dev)
         scratch = torch.empty(int(lib.sl_dst_scratch_bytes()), dtype=torch.uint8, device=dev)
-        N.check(lib.sl_dst_threshold(csr._abi_ref(), self.k_drop, N.ptr(self.thr), N.ptr(scratch), s),
-                "router threshold")
+        N.call("sl_dst_threshold", csr._abi_ref(), self.k_drop, N.ptr(self.thr), N.ptr(scratch), s)
         self.n_keep = torch.empty(csr.nrows, dtype=torch.int32, device=dev)
         self.force = torch.empty(csr.nrows, dtype=torch.int32, device=dev)
-        N.check(lib.sl_dst_keep(csr._abi_ref(), N.ptr(self.thr), N.ptr(self.n_keep),
-                                N.ptr(self.force), s), "router keep")
+        N.call("sl_dst_keep", csr._abi_ref(), N.ptr(self.thr), N.ptr(self.n_keep),
+                                N.ptr(self.force), s)
 
     def finish(self) -> int:
         """Refresh host mirrors; bump the version per rewritten (live) row."""
@@ -187,9 +186,8 @@ class SET(DynamicSparsityAlgorithm):
         dev = csr.device
         off_d = torch.from_numpy(off).to(dev)
         ranks_d = torch.from_numpy(ranks).to(dev)
-        N.check(N.lib().sl_dst_apply_random(csr._abi_ref(), N.ptr(pr.thr), N.ptr(pr.force),
-                                            N.ptr(off_d), N.ptr(ranks_d), csr._stream()),
-                "SET rewrite")
+        N.call("sl_dst_apply_random", csr._abi_ref(), N.ptr(pr.thr), N.ptr(pr.force),
+                                            N.ptr(off_d), N.ptr(ranks_d), csr._stream())
         pr.finish()
 
 
@@ -261,8 +259,8 @@ class RigL(DynamicSparsityAlgorithm):
         flags = torch.empty(csr.nrows, dtype=torch.int32, device=csr.device)
         lib = N.lib()
         s = csr._stream()
-        N.check(lib.sl_dst_apply_topk(csr._abi_ref(), N.ptr(pr.thr), N.ptr(pr.force), N.ptr(G),
-                                      N.ptr(flags), s), "RigL rewrite")
+        N.call("sl_dst_apply_topk", csr._abi_ref(), N.ptr(pr.thr), N.ptr(pr.force), N.ptr(G),
+                                      N.ptr(flags), s)
         flags_h = flags.cpu().numpy()
         flagged = np.nonzero((flags_h != 0) & (csr._rn_h > 0))[0]
         if flagged.size:
@@ -303,9 +301,8 @@ class RigL(DynamicSparsityAlgorithm):
         cols = np.concatenate(lists) if lists else np.zeros(1, np.int32)
         dev = csr.device
         t = [torch.from_numpy(a).to(dev) for a in (mask, off, cols)]
-        N.check(N.lib().sl_dst_apply_cols(csr._abi_ref(), N.ptr(pr.thr), N.ptr(pr.force),
-                                          N.ptr(t[0]), N.ptr(t[1]), N.ptr(t[2]), csr._stream()),
-                "RigL host-resolved rewrite")
+        N.call("sl_dst_apply_cols", csr._abi_ref(), N.ptr(pr.thr), N.ptr(pr.force),
+                                          N.ptr(t[0]), N.ptr(t[1]), N.ptr(t[2]), csr._stream())
 
 
 def dense_grad(dY: torch.Tensor, X: torch.Tensor) -> torch.Tensor:
@@ -324,6 +321,5 @@ def dense_grad(dY: torch.Tensor, X: torch.Tensor) -> torch.Tensor:
     M, Nn = dY.shape
     K = X.shape[0]
     G = torch.empty(M, K, dtype=torch.float32, device=dev)
-    N.check(N.lib().sl_dense_grad(N.ptr(dY), N.ptr(X), M, K, Nn, N.ptr(G), N.stream_ptr(dev)),
-            "dense_grad")
+    N.call("sl_dense_grad", N.ptr(dY), N.ptr(X), M, K, Nn, N.ptr(G), N.stream_ptr(dev))
     return G

@@ -49,13 +49,19 @@ CFG5 = GPTConfig("cfg5-byte-mini-gpt-60M", 768, 8, 12, 512, 256, 3072, 0.7, 0.9,
                  "SET", 200)
 
 
+def _sparse_linear(device):
+    def make(fin, fout, sparsity):
+        return SparseLinear(fin, fout, bias=False, sparsity=sparsity, device=device)
+    return make
+
+
 class CausalSelfAttention(nn.Module):
-    def __init__(self, d_model, n_heads, attn_sparsity, device=None):
+    def __init__(self, d_model, n_heads, attn_sparsity, linear):
         super().__init__()
         self.n_heads = n_heads
         self.d_head = d_model // n_heads
-        self.qkv = SparseLinear(d_model, 3 * d_model, bias=False, sparsity=attn_sparsity, device=device)
-        self.o = SparseLinear(d_model, d_model, bias=False, sparsity=attn_sparsity, device=device)
+        self.qkv = linear(d_model, 3 * d_model, attn_sparsity)
+        self.o = linear(d_model, d_model, attn_sparsity)
 
     def forward(self, x):
         B, T, C = x.shape
@@ -68,22 +74,22 @@ class CausalSelfAttention(nn.Module):
 
 
 class SparseFFN(nn.Module):
-    def __init__(self, d_model, d_ff, sparsity, device=None):
+    def __init__(self, d_model, d_ff, sparsity, linear):
         super().__init__()
-        self.fc_up = SparseLinear(d_model, d_ff, bias=False, sparsity=sparsity, device=device)
-        self.fc_down = SparseLinear(d_ff, d_model, bias=False, sparsity=sparsity, device=device)
+        self.fc_up = linear(d_model, d_ff, sparsity)
+        self.fc_down = linear(d_ff, d_model, sparsity)
 
     def forward(self, x):
         return self.fc_down(F.gelu(self.fc_up(x)))
 
 
 class Block(nn.Module):
-    def __init__(self, cfg: GPTConfig, device=None):
+    def __init__(self, cfg: GPTConfig, linear):
         super().__init__()
         self.ln1 = nn.LayerNorm(cfg.d_model)
-        self.attn = CausalSelfAttention(cfg.d_model, cfg.n_heads, cfg.attn_sparsity, device)
+        self.attn = CausalSelfAttention(cfg.d_model, cfg.n_heads, cfg.attn_sparsity, linear)
         self.ln2 = nn.LayerNorm(cfg.d_model)
-        self.ffn = SparseFFN(cfg.d_model, cfg.d_ff, cfg.ffn_sparsity, device)
+        self.ffn = SparseFFN(cfg.d_model, cfg.d_ff, cfg.ffn_sparsity, linear)
 
     def forward(self, x):
         x = x + self.attn(self.ln1(x))
@@ -92,28 +98,32 @@ class Block(nn.Module):
 
 class MiniGPT(nn.Module):
     """Decoder-only transformer; dense embeddings / LayerNorms / head, sparse
-    attention projections and FFN."""
+    attention projections and FFN.  ``linear(in, out, sparsity)`` builds each
+    sparse projection (default: SparseLinear on ``device``); all parameters
+    are drawn from torch's CPU generator in construction order and the dense
+    parts are then placed on ``device``."""
 
-    def __init__(self, cfg: GPTConfig, device=None):
+    def __init__(self, cfg: GPTConfig, device=None, linear=None):
         super().__init__()
         self.cfg = cfg
+        dev = torch.device(device) if device is not None else None
+        if linear is None:
+            linear = _sparse_linear(device)
+            if dev is None:
+                dev = torch.device("cuda", torch.cuda.current_device())
+        dev = dev or torch.device("cpu")
         self.tok_emb = nn.Embedding(cfg.vocab, cfg.d_model)
         self.pos_emb = nn.Embedding(cfg.seq_len, cfg.d_model)
-        self.blocks = nn.ModuleList([Block(cfg, device) for _ in range(cfg.n_layers)])
+        self.blocks = nn.ModuleList([Block(cfg, linear) for _ in range(cfg.n_layers)])
         self.ln_f = nn.LayerNorm(cfg.d_model)
         self.head = nn.Linear(cfg.d_model, cfg.vocab, bias=False)
         self.register_buffer("pos_ids", torch.arange(cfg.seq_len))
-        dev = next(iter(self.sparse_layers()))._device
-        for name, mod in self.named_children():  # dense parts onto the GPU
-            if name != "blocks":
-                mod.to(dev)
+        for mod in [self.tok_emb, self.pos_emb, self.ln_f, self.head]:
+            mod.to(dev)
         for b in self.blocks:
             b.ln1.to(dev)
             b.ln2.to(dev)
         self.pos_ids = self.pos_ids.to(dev)
-
-    def sparse_layers(self):
-        return (m for m in self.modules() if isinstance(m, SparseLinear))
 
     def forward(self, idx):
         B, T = idx.shape
@@ -123,7 +133,7 @@ class MiniGPT(nn.Module):
         return self.head(self.ln_f(x))
 
 
-def make_mlp(device=None) -> nn.Sequential:
+def make_mlp(device=None) -> nn.Sequential:  # noqa: D401
     """cfg2 MLP: SparseLinear(784,512) -> ReLU -> SparseLinear(512,10)."""
     return nn.Sequential(SparseLinear(784, 512, sparsity=0.9, device=device), nn.ReLU(),
                          SparseLinear(512, 10, sparsity=0.9, device=device))
