@@ -100,6 +100,35 @@ SL_API int sl_transpose_count(const sl_csr* W, double one_plus_padding_ratio,
 SL_API int sl_transpose_fill(const sl_csr* W, const sl_csr* WT, int64_t* perm,
                       const void* scratch, void* stream);
 
+/* Transpose with permutation that allocates nothing.
+ * No counterpart in the reference: it is an addition for callers that cannot
+ * call cudaMalloc -- e.g. code running inside a memory pool or allocator
+ * hook, a real-time loop that forbids allocation, or an embedding host that
+ * owns all device memory -- and so cannot provide the scratch buffer that
+ * sl_transpose_count / sl_transpose_fill need.  Same result as those two
+ * calls (sparselab/layout.py:460 transpose_with_perm), in one call:
+ *   * scratch is a file-scope device array of 4 MiB (2^20 int32 counters)
+ *     that every GPU loading the library holds until the process exits;
+ *     inputs need ceil(nrows/32) * ncols <= 2^20 (and ncols <= 57344), else
+ *     SL_ERR_UNSUPPORTED with a message;
+ *   * WT's row arrays (int32[W.ncols]) receive row_nnz / row_capacity /
+ *     row_start; its slot arrays (values, col_indices) and `perm` must hold
+ *     WT->total_capacity >= floor(one_plus_padding_ratio * W.total_capacity)
+ *     + W.ncols + 2 entries (an upper bound of the true size), else
+ *     SL_ERR_INVALID.  The true total capacity is written to *out_total_dev;
+ *     entries past it are padding (-1, 0.0f, perm -1);
+ *   * the first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture;
+ *   * every call shares the one array and leaves its contents behind (the
+ *     kernels overwrite all of it they read, so nothing must be cleared);
+ *     calls whose work overlaps on the GPU (different streams, or several
+ *     host threads) race on it and give wrong results -- serialise them.
+ * Allocates no device or host memory and calls no allocating routine. */
+SL_API int sl_transpose_with_perm_noalloc(const sl_csr* W, double one_plus_padding_ratio,
+                                   const sl_csr* WT, int64_t* perm,
+                                   int64_t* out_total_dev, void* stream);
+
 /* Cached-transpose value refresh: dst[t] = src[perm[t]] where perm[t] >= 0
  * (sparselab/ops.py:83-94, the cache-hit path of _cached_transpose). */
 SL_API int sl_values_gather(const int64_t* perm, const float* src, float* dst,

@@ -50,6 +50,7 @@ SIGNATURES: dict[str, tuple] = {
     "sl_transpose_count": (I32, [P, F64, P, P, P, P, P, P]),
     "sl_transpose_fill": (I32, [P, P, P, P, P]),
     "sl_values_gather": (I32, [P, P, P, I64, P]),
+    "sl_transpose_with_perm_noalloc": (I32, [P, F64, P, P, P, P]),
     "sl_dense_count": (I32, [P, I64, I64, F32, F64, P, P, P, P, P]),
     "sl_dense_fill": (I32, [P, F32, P, P]),
     "sl_capacity_scan": (I32, [P, I64, F64, P, P, P, P]),
@@ -121,6 +122,7 @@ def ptr(t: torch.Tensor | None) -> P:
 # Kernels each entry point launches (for launch accounting).
 KERNELS_PER_CALL = {
     "sl_spmm_fwd": 1, "sl_sddmm_dw": 1, "sl_transpose_count": 3, "sl_transpose_fill": 2,
+    "sl_transpose_with_perm_noalloc": 5,
     "sl_values_gather": 1, "sl_dense_count": 2, "sl_dense_fill": 1, "sl_capacity_scan": 1,
     "sl_to_dense": 1, "sl_check_invariants": 2, "sl_dense_grad": 1, "sl_dst_threshold": 9,
     "sl_dst_keep": 1, "sl_dst_apply_random": 1, "sl_dst_apply_topk": 1, "sl_dst_apply_cols": 1,

@@ -18,6 +18,10 @@
 //                ascending order: a row's columns are distinct, so every
 //                thread can bump its own column's shared cursor without
 //                contention; a barrier between rows keeps source-row order.
+#include <cmath>
+#include <mutex>
+#include <vector>
+
 #include "common.cuh"
 
 namespace slb {
@@ -207,3 +211,75 @@ int sl_values_gather(const int64_t* perm, const float* src, float* dst, int64_t 
 }
 
 }  // extern "C"
+
+// ── Transpose without any allocation ─────────────────────────────────────
+// For callers that cannot call cudaMalloc (see the header): the per-block
+// column histograms live in this file-scope device array instead of caller
+// scratch.  Every GPU that loads the library holds it until the process
+// exits.  Host code must not pass `g_noalloc_scratch` itself to a kernel:
+// on the host that name is only a stand-in, so its device address is looked
+// up once per device with cudaGetSymbolAddress and cached.
+namespace slb {
+namespace {
+
+constexpr int64_t kNoAllocScratchInts = int64_t(1) << 20;  // 4 MiB per device
+__device__ __align__(256) int32_t g_noalloc_scratch[kNoAllocScratchInts];
+
+int noalloc_scratch(int32_t** out) {
+    static std::mutex mu;
+    static std::vector<int32_t*> addr;
+    int dev = 0;
+    if (int rc = cuda_status(cudaGetDevice(&dev), "sl_transpose_with_perm_noalloc")) return rc;
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= static_cast<int>(addr.size())) addr.resize(dev + 1, nullptr);
+    if (addr[dev] == nullptr) {
+        void* p = nullptr;
+        if (int rc = cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scratch),
+                                 "sl_transpose_with_perm_noalloc: cudaGetSymbolAddress"))
+            return rc;
+        addr[dev] = static_cast<int32_t*>(p);
+    }
+    *out = addr[dev];
+    return SL_OK;
+}
+
+}  // namespace
+}  // namespace slb
+
+extern "C" int sl_transpose_with_perm_noalloc(const sl_csr* W, double one_plus_padding_ratio,
+                                              const sl_csr* WT, int64_t* perm,
+                                              int64_t* out_total_dev, void* stream) {
+    const char* fn = "sl_transpose_with_perm_noalloc";
+    if (int rc = check_csr(W, fn)) return rc;
+    if (WT == nullptr || out_total_dev == nullptr)
+        return fail(SL_ERR_INVALID, std::string(fn) + ": NULL WT or out_total_dev");
+    if (WT->nrows != W->ncols || WT->ncols != W->nrows)
+        return fail(SL_ERR_INVALID, std::string(fn) + ": WT shape must be W's swapped");
+    if (!(one_plus_padding_ratio >= 1.0))
+        return fail(SL_ERR_INVALID, std::string(fn) + ": padding_ratio must be >= 0");
+    const int64_t need_ints = n_blocks(W->nrows > 0 ? W->nrows : 1) * (W->ncols > 0 ? W->ncols : 1);
+    if (need_ints > kNoAllocScratchInts)
+        return fail(SL_ERR_UNSUPPORTED,
+                    std::string(fn) + ": ceil(nrows/32) * ncols = " + std::to_string(need_ints) +
+                        " exceeds the static scratch of " + std::to_string(kNoAllocScratchInts) +
+                        " int32 counters; use sl_transpose_count/sl_transpose_fill with "
+                        "caller-allocated scratch");
+    // Upper bound of the transpose's total capacity: sum_k max(1, ceil(n_k * r))
+    // < r * nnz + ncols + 1 <= r * total_capacity + ncols + 1.
+    const int64_t bound = static_cast<int64_t>(
+                              std::floor(one_plus_padding_ratio * static_cast<double>(W->total_capacity))) +
+                          W->ncols + 2;
+    if (WT->total_capacity < bound)
+        return fail(SL_ERR_INVALID,
+                    std::string(fn) + ": WT slot arrays hold " + std::to_string(WT->total_capacity) +
+                        " entries; at least floor((1+padding_ratio)*total_capacity) + ncols + 2 = " +
+                        std::to_string(bound) + " are required");
+    if (WT->total_capacity > 0 && perm == nullptr)
+        return fail(SL_ERR_INVALID, std::string(fn) + ": NULL perm");
+    int32_t* scratch = nullptr;
+    if (int rc = noalloc_scratch(&scratch)) return rc;
+    if (int rc = sl_transpose_count(W, one_plus_padding_ratio, WT->row_nnz, WT->row_capacity,
+                                    WT->row_start, out_total_dev, scratch, stream))
+        return rc;
+    return sl_transpose_fill(W, WT, perm, scratch, stream);
+}
