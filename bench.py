@@ -92,6 +92,40 @@ def run_kernel_case(spec):
     print(json.dumps({"kernel_case": spec, "M": M, "K": K, "N": N, "nnz": W.nnz}))
 
 
+def graph_time_ms(fn, flush_buf, reps=10):
+    """Device time of one launch of `fn`: CUDA-graph replay of reps x
+    [L2 flush, fn] minus reps x [L2 flush], so neither host launch overhead
+    nor a warm L2 enters the number (flush_buf must exceed the L2)."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+
+    def capture(with_fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(reps):
+                flush_buf.zero_()
+                if with_fn:
+                    fn()
+        return g
+
+    def replay_ms(g):
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        best = float("inf")
+        for _ in range(3):
+            a.record()
+            g.replay()
+            b.record()
+            torch.cuda.synchronize()
+            best = min(best, a.elapsed_time(b))
+        return best
+
+    g1, g0 = capture(True), capture(False)
+    return max(replay_ms(g1) - replay_ms(g0), 1e-6) / reps
+
+
 def run_sweep(args):
     """Config 3: W in {4096x4096, 16384x4096} x sparsity x N; fwd, SDDMM, dX."""
     import sparsecore_b200 as sl
@@ -100,19 +134,10 @@ def run_sweep(args):
     hbm, src, sm_max = peaks()
     fp32 = 148 * 128 * 2 * sm_max * 1e6 / 1e12
 
-    def t_ms(fn, it=10):
-        for _ in range(3):
-            fn()
-        torch.cuda.synchronize()
-        ts = []
-        for _ in range(it):
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            fn()
-            b.record()
-            torch.cuda.synchronize()
-            ts.append(a.elapsed_time(b))
-        return sorted(ts)[len(ts) // 2]
+    flush_buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MB > L2
+
+    def t_ms(fn):
+        return graph_time_ms(fn, flush_buf)
 
     for (M, K) in [(4096, 4096), (16384, 4096)]:
         for s in (0.5, 0.8, 0.9, 0.95, 0.99):

@@ -11,20 +11,26 @@
 // emits it (an in-order vectorised reduction): whole groups of 4 terms as
 // rounded products added one by one, the final (tail mod 4) terms as FMAs.
 //
-// GPU mapping: a quad of 4 lanes evaluates one slot's dot; quad lane q owns
-// chains 4q..4q+3 and reads X[c, 16m+4q .. +3] (and the matching dY) as one
-// 128-bit load per step, so each quad streams a contiguous 64-byte piece of
-// the X row per step.  A CTA of 64 quads works on one row of W at a time
-// (all its quads share the row's dY, which stays L1-resident) and each quad
-// carries S slots of that row concurrently, reusing each dY vector S times.
-// CTAs sweep rows grid-stride.
+// GPU mapping: work items are (row, segment) pairs; a segment is a run of
+// 32 slots of one row, and a row has SPR = ceil(average capacity / 32)
+// segments (segment s of a longer row also takes slots s*32 + k*SPR*32).
+// One warp works on one item at a time, so short rows waste at most one
+// partial segment and long rows still spread over several warps.
+//  * N >= 16 (quad kernel): a quad of 4 lanes evaluates one slot's dot;
+//    quad lane q owns chains 4q..4q+3 and reads X[c, 16m+4q .. +3] (and the
+//    matching dY) as one 128-bit load per step, so each quad streams a
+//    contiguous 64-byte piece of the X row per step; each quad carries S = 4
+//    slots of the row, reusing each dY vector 4 times.
+//  * N < 16 (lane kernel): each lane evaluates one slot's whole dot
+//    (segments of 128 slots, so 4 slots per lane are in flight).
 #include "common.cuh"
 
 namespace slb {
 namespace {
 
 constexpr int kDwThreads = 256;
-constexpr int kQuads = kDwThreads / 4;
+constexpr int kDwWarps = kDwThreads / 32;
+constexpr int kSeg = 32;  // slots per (row, segment) work item and warp pass
 
 template <bool VEC4>
 __device__ __forceinline__ float4 load4(const float* p) {
@@ -52,32 +58,57 @@ __device__ __forceinline__ float4 shfl_xor4(float4 v, int m) {
                        __shfl_xor_sync(0xffffffffu, v.z, m), __shfl_xor_sync(0xffffffffu, v.w, m));
 }
 
-template <bool VEC4, int S>
-__global__ void __launch_bounds__(kDwThreads)
-sddmm_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
-             const int32_t* __restrict__ row_nnz, const int32_t* __restrict__ row_capacity,
-             const int32_t* __restrict__ cols, const float* __restrict__ dY,
-             const float* __restrict__ X, float* __restrict__ dW) {
-    const int q = threadIdx.x & 3;
-    const int quad = threadIdx.x >> 2;
-    const int64_t nfull = N >> 4;
-    const int rem = static_cast<int>(N & 15);
-    const int64_t jtail = nfull * 16 + (rem >= 8 ? 8 : 0);
-    const int64_t jfma = jtail + ((N - jtail) & ~static_cast<int64_t>(3));
+// Scalar tail after the horizontal reduction (see the file comment).
+__device__ __forceinline__ float dot_tail(float r, const float* dyr, const float* xr, int64_t jtail,
+                                          int64_t jfma, int64_t N) {
+    for (int64_t j = jtail; j < jfma; ++j) r = __fadd_rn(r, __fmul_rn(__ldg(dyr + j), __ldg(xr + j)));
+    for (int64_t j = jfma; j < N; ++j) r = fmaf(__ldg(dyr + j), __ldg(xr + j), r);
+    return r;
+}
 
-    for (int row = blockIdx.x; row < M; row += gridDim.x) {
+struct DwShape {
+    int64_t N, nfull, jtail, jfma;
+    int rem;
+    __device__ __forceinline__ explicit DwShape(int64_t n) : N(n) {
+        nfull = n >> 4;
+        rem = static_cast<int>(n & 15);
+        jtail = nfull * 16 + (rem >= 8 ? 8 : 0);
+        jfma = jtail + ((n - jtail) & ~static_cast<int64_t>(3));
+    }
+};
+
+// Zero the padding slots of `row` (lanes of one warp).
+__device__ __forceinline__ void zero_padding(float* dW, int rs, int nn, int cap, int lane) {
+    for (int k = nn + lane; k < cap; k += 32) dW[rs + k] = 0.0f;
+}
+
+template <bool VEC4>
+__global__ void __launch_bounds__(kDwThreads)
+sddmm_quad_kernel(int M, int spr, int64_t N, const int32_t* __restrict__ row_start,
+                  const int32_t* __restrict__ row_nnz, const int32_t* __restrict__ row_capacity,
+                  const int32_t* __restrict__ cols, const float* __restrict__ dY,
+                  const float* __restrict__ X, float* __restrict__ dW) {
+    constexpr int S = 4;
+    const int lane = threadIdx.x & 31;
+    const int q = lane & 3;
+    const int quad = lane >> 2;  // 0..7
+    const DwShape sh(N);
+    const int64_t n_items = static_cast<int64_t>(M) * spr;
+    for (int64_t item = static_cast<int64_t>(blockIdx.x) * kDwWarps + (threadIdx.x >> 5);
+         item < n_items; item += static_cast<int64_t>(gridDim.x) * kDwWarps) {
+        const int row = static_cast<int>(item / spr);
+        const int seg = static_cast<int>(item % spr);
         const int rs = __ldg(row_start + row);
         const int nn = __ldg(row_nnz + row);
-        const int cap = __ldg(row_capacity + row);
-        for (int k = nn + threadIdx.x; k < cap; k += kDwThreads) dW[rs + k] = 0.0f;
+        if (seg == 0) zero_padding(dW, rs, nn, __ldg(row_capacity + row), lane);
         const float* dyr = dY + static_cast<int64_t>(row) * N;
 
-        for (int kb = 0; kb < nn; kb += kQuads * S) {
+        for (int kb = seg * kSeg; kb < nn; kb += spr * kSeg) {
             const float* xr[S];
             bool act[S];
 #pragma unroll
             for (int u = 0; u < S; ++u) {
-                const int k = kb + quad + kQuads * u;
+                const int k = kb + quad + 8 * u;
                 act[u] = k < nn;
                 const int c = act[u] ? __ldg(cols + rs + k) : 0;
                 xr[u] = X + static_cast<int64_t>(c) * N;
@@ -88,7 +119,7 @@ sddmm_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
 
             // 16-wide steps: quad lane q advances chains 4q..4q+3.
 #pragma unroll 2
-            for (int64_t m = 0; m < nfull; ++m) {
+            for (int64_t m = 0; m < sh.nfull; ++m) {
                 const int64_t j = m * 16 + q * 4;
                 const float4 d = load4<VEC4>(dyr + j);
 #pragma unroll
@@ -102,11 +133,12 @@ sddmm_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
                 if (q < 2) acc[u] = add4(acc[u], o);
             }
             // Optional 8-wide step on lanes 0,1 (chains 0-3 and 4-7).
-            if (rem >= 8 && q < 2) {
-                const int64_t j = nfull * 16 + q * 4;
+            if (sh.rem >= 8 && q < 2) {
+                const int64_t j = sh.nfull * 16 + q * 4;
                 const float4 d = load4<VEC4>(dyr + j);
 #pragma unroll
-                for (int u = 0; u < S; ++u) fma4(d, load4<VEC4>(xr[u] + j), acc[u]);
+                for (int u = 0; u < S; ++u)
+                    if (act[u]) fma4(d, load4<VEC4>(xr[u] + j), acc[u]);
             }
             // Horizontal reduction: lane 0 holds acc[0..3], lane 1 acc[4..7].
 #pragma unroll
@@ -115,24 +147,92 @@ sddmm_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
                 if (q == 0 && act[u]) {
                     const float4 s4 = add4(acc[u], hi);
                     float r = __fadd_rn(__fadd_rn(s4.x, s4.z), __fadd_rn(s4.y, s4.w));
-                    for (int64_t j = jtail; j < jfma; ++j)
-                        r = __fadd_rn(r, __fmul_rn(__ldg(dyr + j), __ldg(xr[u] + j)));
-                    for (int64_t j = jfma; j < N; ++j) r = fmaf(__ldg(dyr + j), __ldg(xr[u] + j), r);
-                    dW[rs + kb + quad + kQuads * u] = r;
+                    dW[rs + kb + quad + 8 * u] = dot_tail(r, dyr, xr[u], sh.jtail, sh.jfma, N);
                 }
             }
         }
     }
 }
 
-template <bool VEC4>
+// One slot's whole dot (N < 16: no 16-wide steps, so all 16 chains are +0
+// before the optional 8-wide step).
+__device__ __forceinline__ float lane_dot(const float* dyr, const float* xr, const DwShape& sh) {
+    float a[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) a[t] = __fadd_rn(0.0f, 0.0f);
+    if (sh.rem >= 8)
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+            a[t] = fmaf(__ldg(dyr + sh.nfull * 16 + t), __ldg(xr + sh.nfull * 16 + t), a[t]);
+    float s4[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) s4[t] = __fadd_rn(a[t], a[t + 4]);
+    const float r = __fadd_rn(__fadd_rn(s4[0], s4[2]), __fadd_rn(s4[1], s4[3]));
+    return dot_tail(r, dyr, xr, sh.jtail, sh.jfma, sh.N);
+}
+
+// N < 16: one lane per slot (segments of 128 slots, 4 per lane in flight),
+// all chains in registers.
+constexpr int kLaneSeg = 128;
+__global__ void __launch_bounds__(kDwThreads)
+sddmm_lane_kernel(int M, int spr, int64_t N, const int32_t* __restrict__ row_start,
+                  const int32_t* __restrict__ row_nnz, const int32_t* __restrict__ row_capacity,
+                  const int32_t* __restrict__ cols, const float* __restrict__ dY,
+                  const float* __restrict__ X, float* __restrict__ dW) {
+    const int lane = threadIdx.x & 31;
+    const DwShape sh(N);
+    const int64_t n_items = static_cast<int64_t>(M) * spr;
+    for (int64_t item = static_cast<int64_t>(blockIdx.x) * kDwWarps + (threadIdx.x >> 5);
+         item < n_items; item += static_cast<int64_t>(gridDim.x) * kDwWarps) {
+        const int row = static_cast<int>(item / spr);
+        const int seg = static_cast<int>(item % spr);
+        const int rs = __ldg(row_start + row);
+        const int nn = __ldg(row_nnz + row);
+        if (seg == 0) zero_padding(dW, rs, nn, __ldg(row_capacity + row), lane);
+        const float* dyr = dY + static_cast<int64_t>(row) * N;
+        for (int kb = seg * kLaneSeg; kb < nn; kb += spr * kLaneSeg) {
+            // All four slots' loads are issued before any dot is finished.
+            constexpr int U = kLaneSeg / 32;
+            const float* xr[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int k = kb + u * 32 + lane;
+                xr[u] = X + static_cast<int64_t>(k < nn ? __ldg(cols + rs + k) : 0) * N;
+            }
+            float r[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) r[u] = lane_dot(dyr, xr[u], sh);
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int k = kb + u * 32 + lane;
+                if (k < nn) dW[rs + k] = r[u];
+            }
+        }
+    }
+}
+
 int launch_dw(const sl_csr* W, const float* dY, const float* X, int64_t N, float* dW,
               cudaStream_t s) {
     const int M = static_cast<int>(W->nrows);
-    int blocks = num_sms() * 6;
-    if (blocks > M) blocks = M;
-    sddmm_kernel<VEC4, 4><<<blocks, kDwThreads, 0, s>>>(M, N, W->row_start, W->row_nnz,
-                                                        W->row_capacity, W->col_indices, dY, X, dW);
+    const bool lane_kernel = N < 16;
+    const int seg = lane_kernel ? kLaneSeg : kSeg;
+    const int64_t avg_cap = (W->total_capacity + M - 1) / M;
+    const int spr = static_cast<int>(avg_cap > seg ? (avg_cap + seg - 1) / seg : 1);
+    const int64_t n_items = static_cast<int64_t>(M) * spr;
+    int64_t blocks = (n_items + kDwWarps - 1) / kDwWarps;
+    const int64_t max_blocks = static_cast<int64_t>(num_sms()) * 8;
+    if (blocks > max_blocks) blocks = max_blocks;
+    const bool vec4 = (N % 4 == 0) && aligned16(X) && aligned16(dY);
+    if (lane_kernel) {
+        sddmm_lane_kernel<<<static_cast<unsigned>(blocks), kDwThreads, 0, s>>>(
+            M, spr, N, W->row_start, W->row_nnz, W->row_capacity, W->col_indices, dY, X, dW);
+    } else if (vec4) {
+        sddmm_quad_kernel<true><<<static_cast<unsigned>(blocks), kDwThreads, 0, s>>>(
+            M, spr, N, W->row_start, W->row_nnz, W->row_capacity, W->col_indices, dY, X, dW);
+    } else {
+        sddmm_quad_kernel<false><<<static_cast<unsigned>(blocks), kDwThreads, 0, s>>>(
+            M, spr, N, W->row_start, W->row_nnz, W->row_capacity, W->col_indices, dY, X, dW);
+    }
     SL_RETURN_IF_LAUNCH_FAILED("sl_sddmm_dw");
     return SL_OK;
 }
@@ -150,7 +250,5 @@ extern "C" int sl_sddmm_dw(const sl_csr* W, const float* dY, const float* X, int
     if (dW == nullptr) return fail(SL_ERR_INVALID, "sl_sddmm_dw: NULL dW");
     if (N > 0 && (dY == nullptr || (W->ncols > 0 && X == nullptr)))
         return fail(SL_ERR_INVALID, "sl_sddmm_dw: NULL dense operand");
-    cudaStream_t s = as_stream(stream);
-    const bool vec4 = (N % 4 == 0) && aligned16(X) && aligned16(dY);
-    return vec4 ? launch_dw<true>(W, dY, X, N, dW, s) : launch_dw<false>(W, dY, X, N, dW, s);
+    return launch_dw(W, dY, X, N, dW, as_stream(stream));
 }

@@ -4,27 +4,32 @@
 // over the row's live slots in slot order, starting from +0.  This is the
 // rounding sequence of the reference CPU kernel (csrc/kernels/spmm_avx2.cpp:
 // 82-263, whose 16/8/1-wide stages all perform that same fused update per
-// element), so results are bit-identical.
+// element), so results are bit-identical.  The chain is sequential per
+// element, so parallelism comes only from rows and columns.
 //
 // Work decomposition (gather-bound, no tensor cores): a warp owns a group of
 // RPW = 32/LPR consecutive rows and a tile of TILE = LPR*VEC*CPL columns.
-// Each row of the group is handled by LPR lanes; each lane owns CPL vectors
-// of VEC consecutive columns, strided by LPR*VEC so that the lanes of a row
-// read X rows as contiguous, coalesced 128-bit segments.  The warp stages
-// the (col, value) pairs of its rows' contiguous slot segment through shared
-// memory in chunks (coalesced 32-bit loads), then every lane walks its row's
-// live slots from shared memory (broadcast reads).  Work items (row group,
+// Each row of the group is handled by its own LPR lanes; each lane owns CPL
+// vectors of VEC consecutive columns, strided by LPR*VEC so that the lanes
+// of a row read X rows as contiguous, coalesced 128-bit segments.  All rows
+// of the group advance together: per chunk the warp stages the next CH
+// (col, value) pairs of EVERY row of the group into shared memory with
+// coalesced loads (one row-run of CH slots per load instruction; rows padded
+// to CH+1 pairs so the groups' broadcast reads fall in different banks),
+// then each lane walks its own row's staged slots.  Work items (row group,
 // column tile) are ordered column-tile fastest so that warps resident
 // together share the same W segment (L1/L2 hits) and sweep X once.
+#include <cstdlib>
+#include <cstring>
+
 #include "common.cuh"
 #include "tma.cuh"
 
 namespace slb {
 namespace {
 
-constexpr int kFwdThreads = 256;
-constexpr int kFwdWarps = kFwdThreads / 32;
-constexpr int kChunk = 128;  // staged slots per warp
+constexpr int kFwdWarps = 4;
+constexpr int kFwdThreads = kFwdWarps * 32;
 
 template <int VEC>
 struct Vec;
@@ -49,6 +54,56 @@ __device__ __forceinline__ void fma_vec(float v, float4 x, float* acc) {
 }
 __device__ __forceinline__ void fma_vec(float v, float x, float* acc) { acc[0] = fmaf(v, x, acc[0]); }
 
+// Slot staging.  Per chunk the warp moves slots [base, base+CH) of each of
+// its RPW rows into shared memory (row r at st + r*(CH+1)).  The loads of a
+// chunk go to registers first (ITER = RPW*CH/32 per lane, one row-run of CH
+// slots per warp-wide load), so the next chunk's loads can be in flight while
+// the current chunk is computed.  rs/nn are held by the lanes of each row
+// group (lane r*LPR has row r's).  Slots past a row's nnz are not loaded.
+template <int LPR, int CH>
+struct SlotStager {
+    static constexpr int RPW = 32 / LPR;
+    static constexpr int ITER = RPW * CH / 32;
+    static_assert(ITER * 32 == RPW * CH, "CH must fill whole warp loads");
+    int c[ITER];
+    float v[ITER];
+
+    __device__ __forceinline__ void load(int rs, int nn, int base, const int32_t* __restrict__ cols,
+                                         const float* __restrict__ vals) {
+        const int lane = threadIdx.x & 31;
+#pragma unroll
+        for (int it = 0; it < ITER; ++it) {
+            const int idx = it * 32 + lane;
+            const int r = idx / CH, t = idx % CH;
+            const int r_rs = __shfl_sync(0xffffffffu, rs, r * LPR);
+            const int r_nn = __shfl_sync(0xffffffffu, nn, r * LPR);
+            c[it] = 0;
+            v[it] = 0.0f;
+            if (base + t < r_nn) {
+                c[it] = __ldg(cols + r_rs + base + t);
+                v[it] = __ldg(vals + r_rs + base + t);
+            }
+        }
+    }
+    __device__ __forceinline__ void store(int2* st) const {
+        const int lane = threadIdx.x & 31;
+#pragma unroll
+        for (int it = 0; it < ITER; ++it) {
+            const int idx = it * 32 + lane;
+            st[(idx / CH) * (CH + 1) + idx % CH] = make_int2(c[it], __float_as_int(v[it]));
+        }
+    }
+};
+
+// Staged slots per row per chunk.  Small N (many rows per warp, short
+// compute per chunk): ITER = 16 loads per lane in flight.  Large N (one row
+// per warp, long compute per chunk): ITER = 2 keeps registers for the
+// accumulators.
+template <int LPR>
+struct ChunkOf {
+    static constexpr int value = LPR >= 16 ? 2 * LPR : 16 * LPR;
+};
+
 template <int VEC, int LPR, int CPL>
 __global__ void __launch_bounds__(kFwdThreads)
 spmm_fwd_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
@@ -57,31 +112,28 @@ spmm_fwd_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
                 float* __restrict__ Y, int64_t n_tiles, int64_t n_items) {
     constexpr int RPW = 32 / LPR;
     constexpr int TILE = LPR * VEC * CPL;
-    __shared__ int2 stage[kFwdWarps][kChunk];
+    constexpr int CH = ChunkOf<LPR>::value;
+    __shared__ int2 stage[kFwdWarps][RPW * (CH + 1)];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane / LPR, li = lane % LPR;
+    const int warps_per_block = blockDim.x >> 5;
     int2* st = stage[warp];
+    const int2* my = st + g * (CH + 1);
 
-    for (int64_t item = static_cast<int64_t>(blockIdx.x) * kFwdWarps + warp; item < n_items;
-         item += static_cast<int64_t>(gridDim.x) * kFwdWarps) {
+    for (int64_t item = static_cast<int64_t>(blockIdx.x) * warps_per_block + warp; item < n_items;
+         item += static_cast<int64_t>(gridDim.x) * warps_per_block) {
         const int64_t nt = item % n_tiles;
-        const int row0 = static_cast<int>(item / n_tiles) * RPW;
-        const int row = row0 + g;
+        const int row = static_cast<int>(item / n_tiles) * RPW + g;
         const bool valid = row < M;
         int rs = 0, nn = 0;
         if (valid) {
             rs = __ldg(row_start + row);
             nn = __ldg(row_nnz + row);
         }
-        // Contiguous slot segment covering the live slots of the warp's rows.
-        int lo = (nn > 0) ? rs : INT_MAX;
-        int hi = (nn > 0) ? rs + nn : INT_MIN;
+        int maxnn = nn;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
-            hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
-        }
+        for (int o = 16; o >= LPR; o >>= 1) maxnn = max(maxnn, __shfl_xor_sync(0xffffffffu, maxnn, o));
 
         const int64_t jbase = nt * TILE + static_cast<int64_t>(li) * VEC;
         int64_t jl[CPL];
@@ -96,16 +148,16 @@ spmm_fwd_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
 #pragma unroll
             for (int e = 0; e < VEC; ++e) acc[cc][e] = 0.0f;
 
-        for (int cb = lo; cb < hi; cb += kChunk) {
-            const int cnt = min(kChunk, hi - cb);
-            for (int t = lane; t < cnt; t += 32)
-                st[t] = make_int2(__ldg(cols + cb + t), __float_as_int(__ldg(vals + cb + t)));
+        SlotStager<LPR, CH> sg;
+        if (maxnn > 0) sg.load(rs, nn, 0, cols, vals);
+        for (int base = 0; base < maxnn; base += CH) {
+            sg.store(st);
             __syncwarp();
-            const int s0 = max(rs, cb) - cb;
-            const int s1 = min(rs + nn, cb + cnt) - cb;
-#pragma unroll 4
-            for (int s = s0; s < s1; ++s) {
-                const int2 e = st[s];
+            if (base + CH < maxnn) sg.load(rs, nn, base + CH, cols, vals);  // next chunk in flight
+            const int cnt = min(CH, nn - base);
+#pragma unroll 8
+            for (int t = 0; t < cnt; ++t) {
+                const int2 e = my[t];
                 const float v = __int_as_float(e.y);
                 const float* xr = X + static_cast<int64_t>(e.x) * N;
 #pragma unroll
@@ -132,6 +184,110 @@ spmm_fwd_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
     }
 }
 
+// ── Small N: one row per warp ───────────────────────────────────────────
+// For N < 128 a row's work is short, so rows (not columns) must supply the
+// parallelism: each warp owns one row at a time (M warps in flight).  Per
+// chunk of 32 slots every lane loads one (col, value) pair (coalesced; the
+// next chunk's pair is loaded while the current chunk is consumed) and puts
+// it in the warp's shared-memory slot buffer; the warp then walks the chunk
+// in slot order with broadcast reads; lane j accumulates columns j, j+32,
+// ... (CPL of them).  With N = 1 each lane also gathers X[col] of its own
+// pair up front and the buffer holds (value, x) pairs, read two slots per
+// 128-bit load, so the chain costs half a shared load and one FMA per slot.
+// Same FMA chain per element as above.
+template <int CPL, bool N1>
+__global__ void __launch_bounds__(256)
+spmm_rowwarp_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
+                    const int32_t* __restrict__ row_nnz, const int32_t* __restrict__ cols,
+                    const float* __restrict__ vals, const float* __restrict__ X,
+                    float* __restrict__ Y) {
+    __shared__ __align__(16) int2 buf[8][32];
+    const int lane = threadIdx.x & 31;
+    int2* st = buf[threadIdx.x >> 5];
+    const float4* st4 = reinterpret_cast<const float4*>(st);
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < M; row += warps) {
+        const int rs = __ldg(row_start + row);
+        const int nn = __ldg(row_nnz + row);
+        float acc[CPL];
+#pragma unroll
+        for (int cc = 0; cc < CPL; ++cc) acc[cc] = 0.0f;
+        int c = 0;
+        float v = 0.0f;
+        if (lane < nn) {
+            c = __ldg(cols + rs + lane);
+            v = __ldg(vals + rs + lane);
+        }
+        for (int base = 0; base < nn; base += 32) {
+            if constexpr (N1) {
+                const float x = base + lane < nn ? __ldg(X + c) : 0.0f;
+                st[lane] = make_int2(__float_as_int(v), __float_as_int(x));
+            } else {
+                st[lane] = make_int2(c, __float_as_int(v));
+            }
+            const int nk = base + 32 + lane;  // next chunk's pair in flight
+            if (nk < nn) {
+                c = __ldg(cols + rs + nk);
+                v = __ldg(vals + rs + nk);
+            }
+            __syncwarp();
+            const int cnt = min(32, nn - base);
+            if constexpr (N1) {
+                int t = 0;
+#pragma unroll 8
+                for (; t + 1 < cnt; t += 2) {
+                    const float4 q = st4[t >> 1];
+                    acc[0] = fmaf(q.x, q.y, acc[0]);
+                    acc[0] = fmaf(q.z, q.w, acc[0]);
+                }
+                if (t < cnt) {
+                    const int2 e = st[t];
+                    acc[0] = fmaf(__int_as_float(e.x), __int_as_float(e.y), acc[0]);
+                }
+            } else {
+#pragma unroll 16
+                for (int t = 0; t < cnt; ++t) {
+                    const int2 e = st[t];
+                    const float vt = __int_as_float(e.y);
+                    const float* xr = X + static_cast<int64_t>(e.x) * N;
+#pragma unroll
+                    for (int k = 0; k < CPL; ++k) {
+                        const int64_t j = lane + 32 * k;
+                        if (j < N) acc[k] = fmaf(vt, __ldg(xr + j), acc[k]);
+                    }
+                }
+            }
+            __syncwarp();
+        }
+        float* yr = Y + static_cast<int64_t>(row) * N;
+#pragma unroll
+        for (int k = 0; k < CPL; ++k) {
+            const int64_t j = lane + 32 * k;
+            if (j < N) yr[j] = acc[k];
+        }
+    }
+}
+
+template <int CPL, bool N1>
+int launch_rowwarp(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_t s) {
+    const int M = static_cast<int>(W->nrows);
+    int64_t blocks = (static_cast<int64_t>(M) + 7) / 8;
+    const int64_t max_blocks = static_cast<int64_t>(num_sms()) * 8;
+    if (blocks > max_blocks) blocks = max_blocks;
+    spmm_rowwarp_kernel<CPL, N1><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        M, N, W->row_start, W->row_nnz, W->col_indices, W->values, X, Y);
+    SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd");
+    return SL_OK;
+}
+
+int dispatch_rowwarp(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_t s) {
+    if (N == 1) return launch_rowwarp<1, true>(W, X, N, Y, s);
+    if (N <= 32) return launch_rowwarp<1, false>(W, X, N, Y, s);
+    if (N <= 64) return launch_rowwarp<2, false>(W, X, N, Y, s);
+    if (N <= 96) return launch_rowwarp<3, false>(W, X, N, Y, s);
+    return launch_rowwarp<4, false>(W, X, N, Y, s);
+}
+
 template <int VEC, int LPR, int CPL>
 int launch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_t s) {
     constexpr int RPW = 32 / LPR;
@@ -139,10 +295,14 @@ int launch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_
     const int M = static_cast<int>(W->nrows);
     const int64_t n_tiles = (N + TILE - 1) / TILE;
     const int64_t n_items = ((M + RPW - 1) / RPW) * n_tiles;
-    int64_t blocks = (n_items + kFwdWarps - 1) / kFwdWarps;
-    const int64_t max_blocks = static_cast<int64_t>(num_sms()) * 64;
+    const int sms = num_sms();
+    // Few items: one warp per CTA so that they spread over all SMs.
+    const int threads = n_items < static_cast<int64_t>(sms) * kFwdWarps ? 32 : kFwdThreads;
+    const int wpb = threads / 32;
+    int64_t blocks = (n_items + wpb - 1) / wpb;
+    const int64_t max_blocks = static_cast<int64_t>(sms) * (2048 / threads);
     if (blocks > max_blocks) blocks = max_blocks;
-    spmm_fwd_kernel<VEC, LPR, CPL><<<static_cast<unsigned>(blocks), kFwdThreads, 0, s>>>(
+    spmm_fwd_kernel<VEC, LPR, CPL><<<static_cast<unsigned>(blocks), threads, 0, s>>>(
         M, N, W->row_start, W->row_nnz, W->col_indices, W->values, X, Y, n_tiles, n_items);
     SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd");
     return SL_OK;
@@ -167,12 +327,15 @@ int dispatch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStrea
 // shared memory -- loaded by TMA as 128-row boxes completing on one mbarrier
 // -- and streams rows of W against it: every FMA's X operand then comes from
 // shared memory (one conflict-free 128-bit read per lane per slot) instead
-// of L2.  Work items are (column tile, block of rows), tile-major; each CTA
-// takes a contiguous run of items and reloads X only when its tile changes.
+// of L1/L2.  Lanes are laid out as in spmm_fwd_kernel with VEC = 4, CPL = 1
+// (LPR = TN/4 lanes per row, all rows of a warp advancing together).  Work
+// items are (column tile, block of rows), tile-major; each CTA takes a
+// contiguous run of items and reloads X only when its tile changes.
 // Numerics are identical to spmm_fwd_kernel (same per-element FMA chain).
 constexpr int kXsThreads = 512;
 constexpr int kXsWarps = kXsThreads / 32;
 constexpr int kXsBoxRows = 128;
+constexpr int kXsCh = 16;  // staged slots per row per chunk (TN = 32: 4 rows per warp)
 constexpr int kXsRowsPerItemMul = 4;
 
 template <int LPR>
@@ -192,7 +355,8 @@ spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane / LPR, li = lane % LPR;
-    int2* st = stage + warp * kChunk;
+    int2* st = stage + warp * RPW * (kXsCh + 1);
+    const int2* my = st + g * (kXsCh + 1);
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
         fence_barrier_init();
@@ -223,6 +387,7 @@ spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
             cur_tile = tile;
         }
         const int64_t j = tile * TN + li * 4;
+        const float* xcol = xs + li * 4;
         for (int rg = warp; rg < ROWS_PER_ITEM / RPW; rg += kXsWarps) {
             const int row = chunk * ROWS_PER_ITEM + rg * RPW + g;
             const bool valid = row < M;
@@ -231,25 +396,22 @@ spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
                 rs = __ldg(row_start + row);
                 nn = __ldg(row_nnz + row);
             }
-            int lo = (nn > 0) ? rs : INT_MAX;
-            int hi = (nn > 0) ? rs + nn : INT_MIN;
+            int maxnn = nn;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
-                hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
-            }
+            for (int o = 16; o >= LPR; o >>= 1)
+                maxnn = max(maxnn, __shfl_xor_sync(0xffffffffu, maxnn, o));
             float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int cb = lo; cb < hi; cb += kChunk) {
-                const int cnt = min(kChunk, hi - cb);
-                for (int t = lane; t < cnt; t += 32)
-                    st[t] = make_int2(__ldg(cols + cb + t), __float_as_int(__ldg(vals + cb + t)));
+            SlotStager<LPR, kXsCh> sg;
+            if (maxnn > 0) sg.load(rs, nn, 0, cols, vals);
+            for (int base = 0; base < maxnn; base += kXsCh) {
+                sg.store(st);
                 __syncwarp();
-                const int s0 = max(rs, cb) - cb;
-                const int s1 = min(rs + nn, cb + cnt) - cb;
-#pragma unroll 4
-                for (int s = s0; s < s1; ++s) {
-                    const int2 e = st[s];
-                    const float4 x = *reinterpret_cast<const float4*>(xs + e.x * TN + li * 4);
+                if (base + kXsCh < maxnn) sg.load(rs, nn, base + kXsCh, cols, vals);
+                const int cnt = min(kXsCh, nn - base);
+#pragma unroll 8
+                for (int t = 0; t < cnt; ++t) {
+                    const int2 e = my[t];
+                    const float4 x = *reinterpret_cast<const float4*>(xcol + e.x * TN);
                     fma_vec(__int_as_float(e.y), x, acc);
                 }
                 __syncwarp();
@@ -264,11 +426,10 @@ spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
 // Tile width by K so that the resident tile fits in shared memory.
 int xs_lanes_for(int64_t K) {
     const int64_t rows = (K + kXsBoxRows - 1) / kXsBoxRows * kXsBoxRows;
-    const int64_t budget = 200 * 1024;
-    if (rows * 32 * 4 <= budget) return 8;   // TN = 32
-    if (rows * 16 * 4 <= budget) return 4;   // TN = 16
-    if (rows * 8 * 4 <= budget) return 2;    // TN = 8
-    return 0;
+    const int64_t budget = 192 * 1024;
+    // Narrower tiles put more rows on a warp and lose to the row-gather
+    // kernel (measured on B200), so only TN = 32 is used.
+    return rows * 32 * 4 <= budget ? 8 : 0;
 }
 
 template <int LPR>
@@ -283,14 +444,14 @@ int launch_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, c
     const int M = static_cast<int>(W->nrows);
     const int nbox = static_cast<int>((K + kXsBoxRows - 1) / kXsBoxRows);
     const size_t smem = static_cast<size_t>(nbox) * kXsBoxRows * TN * 4 +
-                        static_cast<size_t>(kXsWarps) * kChunk * sizeof(int2);
+                        static_cast<size_t>(kXsWarps) * RPW * (kXsCh + 1) * sizeof(int2);
     if (cudaFuncSetAttribute(spmm_xs_kernel<LPR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
         return -1;
     const int row_chunks = (M + ROWS_PER_ITEM - 1) / ROWS_PER_ITEM;
     const int64_t n_tiles = (N + TN - 1) / TN;
     const int64_t n_items = n_tiles * row_chunks;
-    const int per_sm = smem <= 110 * 1024 ? 2 : 1;
+    const int per_sm = smem <= 112 * 1024 ? 2 : 1;
     int64_t grid = static_cast<int64_t>(num_sms()) * per_sm;
     if (grid > n_items) grid = n_items;
     const int64_t per_cta = (n_items + grid - 1) / grid;
@@ -302,15 +463,20 @@ int launch_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, c
     return SL_OK;
 }
 
+// SPARSECORE_B200_FWD=rows|xs forces one forward path (tuning and tests);
+// by default the X-stationary path runs where it applies.
+enum { kPathAuto = 0, kPathRows = 1, kPathXs = 2 };
+int fwd_path() {
+    const char* e = std::getenv("SPARSECORE_B200_FWD");
+    if (e && std::strcmp(e, "rows") == 0) return kPathRows;
+    if (e && std::strcmp(e, "xs") == 0) return kPathXs;
+    return kPathAuto;
+}
+
 // Returns -1 when the X-stationary path does not apply.
 int try_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, cudaStream_t s) {
     if (N < 256 || N % 4 != 0 || !aligned16(X) || !aligned16(Y) || K < 1 || K > INT_MAX) return -1;
-    switch (xs_lanes_for(K)) {
-        case 8: return launch_xs<8>(W, X, K, N, Y, s);
-        case 4: return launch_xs<4>(W, X, K, N, Y, s);
-        case 2: return launch_xs<2>(W, X, K, N, Y, s);
-        default: return -1;
-    }
+    return xs_lanes_for(K) == 8 ? launch_xs<8>(W, X, K, N, Y, s) : -1;
 }
 }  // namespace
 }  // namespace slb
@@ -332,8 +498,11 @@ extern "C" int sl_spmm_fwd(const sl_csr* W, const float* X, int64_t K, int64_t N
     cudaStream_t s = as_stream(stream);
     if (K == 0) return cuda_status(cudaMemsetAsync(Y, 0, sizeof(float) * W->nrows * N, s),
                                    "sl_spmm_fwd memset");
-    const int rc = try_xs(W, X, K, N, Y, s);
-    if (rc >= 0) return rc;
+    if (fwd_path() != kPathRows) {
+        const int rc = try_xs(W, X, K, N, Y, s);
+        if (rc >= 0) return rc;
+    }
+    if (N < 128) return dispatch_rowwarp(W, X, N, Y, s);
     const bool vec4 = (N % 4 == 0) && aligned16(X) && aligned16(Y);
     return vec4 ? dispatch_fwd<4>(W, X, N, Y, s) : dispatch_fwd<1>(W, X, N, Y, s);
 }

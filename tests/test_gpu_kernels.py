@@ -157,3 +157,33 @@ def test_transpose_involution_and_padding_ratio():
     assert W0.padding_slots == int((host(W0.row_nnz) == 0).sum())
     with pytest.raises(ValueError):
         W.transpose(padding_ratio=-1.0)
+
+
+@pytest.mark.parametrize("path", ["rows", "xs"])
+def test_forward_paths_and_sddmm_variants_vs_oracle(path, monkeypatch):
+    """Both forward decompositions (row-gather and X-stationary), the lane and
+    quad SDDMM kernels, ragged row lengths (one dense row among sparse ones,
+    empty rows) and column counts around every dispatch threshold."""
+    import sparsecore_b200 as sl
+    from oracle import oracle as O
+    from sparsecore_b200 import ops
+
+    monkeypatch.setenv("SPARSECORE_B200_FWD", path)
+    d = dev()
+    g = torch.Generator().manual_seed(11)
+    M, K = 301, 517
+    mask = torch.rand(M, K, generator=g) < 0.1
+    mask[7] = True          # one dense row: several segments per warp pass
+    mask[100:140] = False   # empty rows
+    Wd = torch.randn(M, K, generator=g) * mask
+    W = sl.PaddedCSR.from_dense(Wd.to(d))
+    Wo = oracle_csr(W)
+    WT, _ = sl.transpose_with_perm(W)
+    WTo, _ = O.transpose_with_perm(Wo)
+    for N in (1, 3, 4, 8, 12, 20, 36, 63, 64, 68, 252, 256, 260, 384, 1000):
+        X = torch.randn(K, N, generator=g)
+        dY = torch.randn(M, N, generator=g)
+        Xd, dYd = X.to(d), dY.to(d)
+        assert bits_equal(sl.spmm(W, Xd), O.spmm(Wo, X.numpy())), N
+        assert bits_equal(ops._sddmm_raw(W, dYd, Xd), O.sddmm(Wo, dY.numpy(), X.numpy())), N
+        assert bits_equal(ops._spmm_raw(WT, dYd), O.spmm(WTo, dY.numpy())), N
