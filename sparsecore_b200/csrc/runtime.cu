@@ -126,7 +126,7 @@ unpack_live_kernel(int M, const int32_t* __restrict__ row_start,
 }
 
 bool make_tmap_2d(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int box_rows,
-                  int box_cols) {
+                  int box_cols, bool swizzle128) {
     static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     static std::once_flag once;
     std::call_once(once, [] {
@@ -143,7 +143,8 @@ bool make_tmap_2d(CUtensorMap* map, const float* base, int64_t rows, int64_t col
     const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
     const cuuint32_t estr[2] = {1, 1};
     return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }

@@ -23,7 +23,11 @@
 //    slots of the row, reusing each dY vector 4 times.
 //  * N < 16 (lane kernel): each lane evaluates one slot's whole dot
 //    (segments of 128 slots, so 4 slots per lane are in flight).
+#include <cmath>
+#include <cstdlib>
+
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace slb {
 namespace {
@@ -211,6 +215,224 @@ sddmm_lane_kernel(int M, int spr, int64_t N, const int32_t* __restrict__ row_sta
     }
 }
 
+// ── Tiled SDDMM (large N, N % 32 == 0) ───────────────────────────────────
+// The per-slot kernels above gather X[col] from L2 once per slot, so they are
+// bound by L2 bandwidth.  Here a CTA owns a 2-D tile of W (TR rows x TC
+// columns) and streams the two operand blocks dY[tile rows, :] and
+// X[tile cols, :] through shared memory in 32-column chunks (TMA, 128-byte
+// swizzle, double-buffered on two mbarriers).  The tile's live slots keep
+// their 16 chains in registers for the whole sweep over N (quad layout as
+// above: quad lane q owns chains 4q..4q+3), so every operand element is
+// fetched from L2 once per tile instead of once per slot.  A tile holding
+// more than 512 slots sweeps N once per batch of 512.  Same rounding
+// sequence as the other SDDMM kernels (N % 16 == 0: no 8-wide step, no tail).
+constexpr int kTThreads = 256;
+constexpr int kTQuads = kTThreads / 4;
+constexpr int kTS = 8;                    // slots per quad per batch
+constexpr int kTBatch = kTQuads * kTS;    // 512
+constexpr int kTJ = 32;                   // columns per chunk: 128-byte rows
+constexpr int kTMaxRows = 128;
+constexpr int kTCols = 64;
+constexpr int kTStages = 6;
+
+// Float offset of float4 `chunk` (0..7) of `row` in a 128B-swizzled tile.
+__device__ __forceinline__ int sw(int row, int chunk) { return row * kTJ + ((chunk ^ (row & 7)) << 2); }
+
+__device__ __forceinline__ int lower_bound_cols(const int32_t* __restrict__ c, int n, int key) {
+    int lo = 0, hi = n;
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (__ldg(c + mid) < key) lo = mid + 1; else hi = mid;
+    }
+    return lo;
+}
+
+__global__ void __launch_bounds__(kTThreads + 32, 2)
+sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_constant__ CUtensorMap xmap,
+                   int M, int64_t N, int TR, int TC, int n_bc,
+                   const int32_t* __restrict__ row_start, const int32_t* __restrict__ row_nnz,
+                   const int32_t* __restrict__ row_capacity, const int32_t* __restrict__ cols,
+                   float* __restrict__ dW, unsigned* status) {
+    extern __shared__ unsigned char smem_raw[];
+    float* sbase = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ __align__(8) uint64_t full[kTStages];
+    __shared__ __align__(8) uint64_t empty[kTStages];
+    __shared__ int run_lo[kTMaxRows];
+    __shared__ int run_pref[kTMaxRows + 1];
+    __shared__ int ws[(kTThreads + 32) / 32];
+    __shared__ int slot_of[kTBatch];  // global slot of each batch position (-1 = none)
+
+    const int tid = threadIdx.x, lane = tid & 31, q = lane & 3, quad = tid >> 2;
+    const bool producer = tid >= kTThreads;  // warp 8 issues the copies
+    const int bi = blockIdx.x / n_bc, bc = blockIdx.x % n_bc;
+    const int r0 = bi * TR, c0 = bc * TC;
+    const int nrows = min(TR, M - r0);
+
+    // Each tile row's live slots in [c0, c0+TC) are one run of its sorted row.
+    int cnt = 0;
+    if (tid < nrows) {
+        const int rs = __ldg(row_start + r0 + tid), nn = __ldg(row_nnz + r0 + tid);
+        const int lo = lower_bound_cols(cols + rs, nn, c0);
+        const int hi = lo + lower_bound_cols(cols + rs + lo, nn - lo, c0 + TC);
+        run_lo[tid] = rs + lo;
+        cnt = hi - lo;
+    }
+    int total;
+    const int ex = block_exclusive_scan<kTThreads + 32>(cnt, ws, &total);
+    if (tid < TR) run_pref[tid] = ex;
+    if (tid == 0) run_pref[TR] = total;
+    if (bc == 0) {  // padding slots of the tile's rows -> 0
+        for (int r = tid >> 5; r < nrows; r += (kTThreads + 32) / 32) {
+            const int rs = __ldg(row_start + r0 + r);
+            for (int k = __ldg(row_nnz + r0 + r) + lane; k < __ldg(row_capacity + r0 + r); k += 32)
+                dW[rs + k] = 0.0f;
+        }
+    }
+    if (tid == 0) {
+        for (int b = 0; b < kTStages; ++b) {
+            mbar_init(&full[b], 1);
+            mbar_init(&empty[b], kTThreads / 32);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (total == 0) return;
+
+    // Stage b: dY block at sbase + b*stage, X block right after it.
+    const int stage = (TR + TC) * kTJ;
+    const int nchunks = static_cast<int>(N / kTJ);
+    const int nbatch = (total + kTBatch - 1) / kTBatch;
+    const int nsteps = nbatch * nchunks;  // step g = batch * nchunks + chunk
+
+    if (producer) {
+        if (lane == 0) {
+            const unsigned chunk_bytes = static_cast<unsigned>(stage * 4);
+            unsigned eph = 0u;  // bit b = parity of stage b's next release
+            int g = 0;
+            for (; g < nsteps; ++g) {
+                const int b = g % kTStages;
+                if (g >= kTStages) {
+                    if (!mbar_wait(&empty[b], (eph >> b) & 1u, status)) break;
+                    eph ^= 1u << b;
+                }
+                const int k = g % nchunks;
+                fence_proxy_async();
+                mbar_expect_tx(&full[b], chunk_bytes);
+                tma_load_2d(sbase + b * stage, &dymap, k * kTJ, r0, &full[b]);
+                tma_load_2d(sbase + b * stage + TR * kTJ, &xmap, k * kTJ, c0, &full[b]);
+            }
+            // Before the CTA may exit, every issued copy must have landed:
+            // wait (bounded) for the full-barrier completion of the last
+            // kTStages issued steps.
+            const int g0 = g > kTStages ? g - kTStages : 0;
+            for (int h = g0; h < g; ++h) mbar_wait(&full[h % kTStages], (h / kTStages) & 1u, status);
+        }
+        return;
+    }
+
+    unsigned fph = 0u;  // bit b = parity of stage b's next fill
+    for (int bt = 0; bt < nbatch; ++bt) {
+        const int b0 = bt * kTBatch;
+        // Per slot: swizzled float offsets of its dY row and X row for the
+        // chunk's first 16 columns (the second 16 are the same ^ 16), packed
+        // as (dY << 16) | X; `fresh` bit s = slot s starts a new W row.
+        int off[kTS];
+        unsigned fresh = 0u;
+        int prev_r = -1;
+#pragma unroll
+        for (int s = 0; s < kTS; ++s) {
+            const int t = b0 + quad * kTS + s;
+            int r = 0, c = 0, sl = -1;
+            if (t < total) {
+                int lo = 0, hi = TR;  // last r with run_pref[r] <= t
+                while (hi - lo > 1) {
+                    const int mid = (lo + hi) >> 1;
+                    if (run_pref[mid] <= t) lo = mid; else hi = mid;
+                }
+                sl = run_lo[lo] + (t - run_pref[lo]);
+                r = lo;
+                c = __ldg(cols + sl) - c0;
+            }
+            if (q == 0) slot_of[quad * kTS + s] = sl;
+            const int yo = r * kTJ + ((q ^ (r & 7)) << 2);
+            const int xo = TR * kTJ + c * kTJ + ((q ^ (c & 7)) << 2);
+            off[s] = (yo << 16) | xo;
+            if (s == 0 || r != prev_r) fresh |= 1u << s;
+            prev_r = r;
+        }
+        float4 acc[kTS];
+#pragma unroll
+        for (int s = 0; s < kTS; ++s) acc[s] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+        for (int k = 0; k < nchunks; ++k) {
+            const int b = (bt * nchunks + k) % kTStages;
+            if (!mbar_wait(&full[b], (fph >> b) & 1u, status)) return;  // bounded; status raised
+            fph ^= 1u << b;
+            const float* sb = sbase + b * stage;
+            float4 d0 = make_float4(0.f, 0.f, 0.f, 0.f), d1 = d0;
+#pragma unroll
+            for (int s = 0; s < kTS; ++s) {
+                const int yo = off[s] >> 16, xo = off[s] & 0xffff;
+                if (fresh & (1u << s)) {
+                    d0 = *reinterpret_cast<const float4*>(sb + yo);
+                    d1 = *reinterpret_cast<const float4*>(sb + (yo ^ 16));
+                }
+                const float4 x0 = *reinterpret_cast<const float4*>(sb + xo);
+                const float4 x1 = *reinterpret_cast<const float4*>(sb + (xo ^ 16));
+                fma4(d0, x0, acc[s]);
+                fma4(d1, x1, acc[s]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[b]);  // this warp is done with stage b
+        }
+        // acc = acc_a + acc_b, then the horizontal reduction (N % 16 == 0).
+#pragma unroll
+        for (int s = 0; s < kTS; ++s) {
+            const float4 o = shfl_xor4(acc[s], 2);
+            if (q < 2) acc[s] = add4(acc[s], o);
+            const float4 hi = shfl_xor4(acc[s], 1);
+            const int sl = q == 0 ? slot_of[quad * kTS + s] : -1;
+            if (sl >= 0) {
+                const float4 s4 = add4(acc[s], hi);
+                dW[sl] = __fadd_rn(__fadd_rn(s4.x, s4.z), __fadd_rn(s4.y, s4.w));
+            }
+        }
+    }
+}
+
+// Returns -1 when the tiled path does not apply.
+int try_tiled(const sl_csr* W, const float* dY, const float* X, int64_t N, float* dW, cudaStream_t s) {
+    const int64_t M = W->nrows, K = W->ncols;
+    if (N < 256 || N % kTJ != 0 || !aligned16(dY) || !aligned16(X) || N > INT_MAX / 2) return -1;
+    // Live density estimate from the capacity (live + about 20% padding).
+    const double dens = static_cast<double>(W->total_capacity) / 1.2 / (static_cast<double>(M) * K);
+    if (dens < 0.02) return -1;
+    int TR = static_cast<int>(std::floor(480.0 / (kTCols * dens) / 8.0)) * 8;
+    TR = TR < 8 ? 8 : (TR > kTMaxRows ? kTMaxRows : TR);
+    const int TC = kTCols;
+    unsigned* status = device_status_word();
+    if (status == nullptr) return -1;
+    CUtensorMap dymap, xmap;
+    if (!make_tmap_2d(&dymap, dY, M, N, TR, kTJ, true) || !make_tmap_2d(&xmap, X, K, N, TC, kTJ, true))
+        return -1;
+    const size_t smem = static_cast<size_t>(kTStages * (TR + TC) * kTJ * 4) + 1024;
+    if (cudaFuncSetAttribute(sddmm_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+        return -1;
+    const int n_bi = static_cast<int>((M + TR - 1) / TR), n_bc = static_cast<int>((K + TC - 1) / TC);
+    sddmm_tiled_kernel<<<n_bi * n_bc, kTThreads + 32, smem, s>>>(
+        dymap, xmap, static_cast<int>(M), N, TR, TC, n_bc, W->row_start, W->row_nnz,
+        W->row_capacity, W->col_indices, dW, status);
+    SL_RETURN_IF_LAUNCH_FAILED("sl_sddmm_dw (tiled)");
+    return SL_OK;
+}
+
+// SPARSECORE_B200_DW=quad forces the per-slot kernels (tuning and tests).
+bool tiled_disabled() {
+    const char* e = std::getenv("SPARSECORE_B200_DW");
+    return e != nullptr && e[0] == 'q';
+}
+
 int launch_dw(const sl_csr* W, const float* dY, const float* X, int64_t N, float* dW,
               cudaStream_t s) {
     const int M = static_cast<int>(W->nrows);
@@ -250,5 +472,10 @@ extern "C" int sl_sddmm_dw(const sl_csr* W, const float* dY, const float* X, int
     if (dW == nullptr) return fail(SL_ERR_INVALID, "sl_sddmm_dw: NULL dW");
     if (N > 0 && (dY == nullptr || (W->ncols > 0 && X == nullptr)))
         return fail(SL_ERR_INVALID, "sl_sddmm_dw: NULL dense operand");
-    return launch_dw(W, dY, X, N, dW, as_stream(stream));
+    cudaStream_t s = as_stream(stream);
+    if (!tiled_disabled() && W->ncols > 0) {
+        const int rc = try_tiled(W, dY, X, N, dW, s);
+        if (rc >= 0) return rc;
+    }
+    return launch_dw(W, dY, X, N, dW, s);
 }

@@ -379,7 +379,10 @@ spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
                     tma_load_2d(xs + static_cast<size_t>(b) * kXsBoxRows * TN, &xmap,
                                 static_cast<int>(tile * TN), b * kXsBoxRows, &bar);
             }
-            if (!mbar_wait(&bar, phase, status)) {
+            // Bounded wait; all threads agree at the barrier whether any gave
+            // up, so that they leave together.
+            const bool ok = mbar_wait(&bar, phase, status);
+            if (__syncthreads_or(!ok)) {
                 mbar_wait(&bar, phase, status);  // let copies in flight land, then leave
                 return;
             }

@@ -18,7 +18,7 @@ namespace slb {
 // [box_rows, box_cols].  Returns false if the driver entry point is missing
 // or the encode fails (caller falls back to the non-TMA kernel).
 bool make_tmap_2d(CUtensorMap* map, const float* base, int64_t rows, int64_t cols,
-                  int box_rows, int box_cols);
+                  int box_rows, int box_cols, bool swizzle128 = false);
 
 // Per-device status word owned by the library (bit 0 = a bounded wait timed
 // out); allocated on first use on the current device.
@@ -47,6 +47,11 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
                  "r"(bytes)
                  : "memory");
+}
+
+// Plain arrive (one count) on an mbarrier.
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
 // Returns false on timeout (and raises bit 0 of *status).

@@ -187,3 +187,29 @@ def test_forward_paths_and_sddmm_variants_vs_oracle(path, monkeypatch):
         assert bits_equal(sl.spmm(W, Xd), O.spmm(Wo, X.numpy())), N
         assert bits_equal(ops._sddmm_raw(W, dYd, Xd), O.sddmm(Wo, dY.numpy(), X.numpy())), N
         assert bits_equal(ops._spmm_raw(WT, dYd), O.spmm(WTo, dY.numpy())), N
+
+
+@pytest.mark.parametrize("M,K,N,block", [(301, 517, 256, False), (700, 300, 512, True),
+                                         (96, 2000, 288, False), (1000, 1000, 320, True)])
+def test_tiled_sddmm_matches_slot_kernels_and_oracle(M, K, N, block, monkeypatch):
+    """The tiled SDDMM (large N) against the per-slot kernels and the oracle:
+    edge tiles (M, K not multiples of the tile), and a dense block that puts
+    thousands of slots into one tile (several batches per tile)."""
+    import sparsecore_b200 as sl
+    from oracle import oracle as O
+    from sparsecore_b200 import ops
+
+    d = dev()
+    g = torch.Generator().manual_seed(M + K)
+    mask = torch.rand(M, K, generator=g) < 0.06
+    if block:
+        mask[:130, :70] = True
+    Wd = torch.randn(M, K, generator=g) * mask
+    W = sl.PaddedCSR.from_dense(Wd.to(d))
+    X = torch.randn(K, N, generator=g)
+    dY = torch.randn(M, N, generator=g)
+    tiled = ops._sddmm_raw(W, dY.to(d), X.to(d))
+    monkeypatch.setenv("SPARSECORE_B200_DW", "quad")
+    per_slot = ops._sddmm_raw(W, dY.to(d), X.to(d))
+    assert bits_equal(tiled, per_slot)
+    assert bits_equal(tiled, O.sddmm(oracle_csr(W), dY.numpy(), X.numpy()))
