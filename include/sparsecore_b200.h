@@ -209,6 +209,15 @@ SL_API int sl_dst_apply_cols(const sl_csr* W, const float* thr_dev,
                       const int32_t* grow_offsets, const int32_t* grow_cols,
                       void* stream);
 
+/* ── Dense layout helper ──────────────────────────────────────────────────
+ * dst[cols, rows] = src[rows, cols]^T (fp32, row-major, not in place).
+ * Replaces the torch copies of the reference's SparseLinear
+ * (sparselab/nn.py:229-237: x.reshape(-1, in).t().contiguous() and the .t()
+ * of the result): activations stay token-major [tokens, features] outside
+ * the layer and column-per-token [features, tokens] for the kernels. */
+SL_API int sl_transpose_f32(const float* src, int64_t rows, int64_t cols, float* dst,
+                     void* stream);
+
 /* ── Data-parallel packing of live gradient slots ────────────────────────
  * packed_offsets[nrows] = exclusive scan of row_nnz.  pack copies the live
  * slots of src[total_capacity] into dst[nnz]; unpack scatters back into

@@ -67,6 +67,7 @@ SIGNATURES: dict[str, tuple] = {
     "sl_pack_live": (I32, [P, P, P, P, P]),
     "sl_unpack_live": (I32, [P, P, P, P, F32, P]),
     "sl_exclusive_scan": (I32, [P, I64, P, P, P]),
+    "sl_transpose_f32": (I32, [P, I64, I64, P, P]),
 }
 
 _lib = None

@@ -1,0 +1,60 @@
+// Dense fp32 transpose for the SparseLinear layout change (token-major
+// activations [N, K] <-> the kernels' column-per-token operands [K, N]).
+// The reference does this with torch copies (sparselab/nn.py:229-237:
+// x.reshape(-1, in).t().contiguous() and the .t() of the result).
+//
+// 32 x 32 tiles through shared memory (row padded to 33 floats: the
+// column-wise reads hit 32 different banks); 256 threads per tile, each
+// moving 4 elements in and 4 out, both directions coalesced.
+#include "common.cuh"
+
+namespace slb {
+namespace {
+
+constexpr int kTile = 32;
+constexpr int kRowsPerPass = 8;
+
+__global__ void __launch_bounds__(kTile * kRowsPerPass)
+transpose_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
+                 float* __restrict__ dst, int64_t tiles_c, int64_t n_tiles) {
+    __shared__ float t[kTile][kTile + 1];
+    const int tx = threadIdx.x & (kTile - 1), ty = threadIdx.x / kTile;
+    for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        const int64_t r0 = (tile / tiles_c) * kTile, c0 = (tile % tiles_c) * kTile;
+#pragma unroll
+        for (int k = 0; k < kTile; k += kRowsPerPass) {
+            const int64_t r = r0 + ty + k, c = c0 + tx;
+            if (r < rows && c < cols) t[ty + k][tx] = __ldg(src + r * cols + c);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < kTile; k += kRowsPerPass) {
+            const int64_t c = c0 + ty + k, r = r0 + tx;  // dst row c, column r
+            if (c < cols && r < rows) dst[c * rows + r] = t[tx][ty + k];
+        }
+        __syncthreads();
+    }
+}
+
+}  // namespace
+}  // namespace slb
+
+using namespace slb;
+
+extern "C" int sl_transpose_f32(const float* src, int64_t rows, int64_t cols, float* dst,
+                                void* stream) {
+    if (rows < 0 || cols < 0) return fail(SL_ERR_INVALID, "sl_transpose_f32: negative shape");
+    if (rows == 0 || cols == 0) return SL_OK;
+    if (src == nullptr || dst == nullptr)
+        return fail(SL_ERR_INVALID, "sl_transpose_f32: NULL operand");
+    if (src == dst) return fail(SL_ERR_INVALID, "sl_transpose_f32: in-place is not supported");
+    const int64_t tiles_c = (cols + kTile - 1) / kTile;
+    const int64_t n_tiles = ((rows + kTile - 1) / kTile) * tiles_c;
+    int64_t grid = n_tiles;
+    const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
+    if (grid > cap) grid = cap;
+    transpose_kernel<<<static_cast<unsigned>(grid), kTile * kRowsPerPass, 0, as_stream(stream)>>>(
+        src, rows, cols, dst, tiles_c, n_tiles);
+    SL_RETURN_IF_LAUNCH_FAILED("sl_transpose_f32");
+    return SL_OK;
+}

@@ -232,8 +232,7 @@ constexpr int kTS = 8;                    // slots per quad per batch
 constexpr int kTBatch = kTQuads * kTS;    // 512
 constexpr int kTJ = 32;                   // columns per chunk: 128-byte rows
 constexpr int kTMaxRows = 128;
-constexpr int kTCols = 64;
-constexpr int kTStages = 6;
+constexpr int kTStages = 5;
 
 // Float offset of float4 `chunk` (0..7) of `row` in a 128B-swizzled tile.
 __device__ __forceinline__ int sw(int row, int chunk) { return row * kTJ + ((chunk ^ (row & 7)) << 2); }
@@ -377,10 +376,8 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
                     d0 = *reinterpret_cast<const float4*>(sb + yo);
                     d1 = *reinterpret_cast<const float4*>(sb + (yo ^ 16));
                 }
-                const float4 x0 = *reinterpret_cast<const float4*>(sb + xo);
-                const float4 x1 = *reinterpret_cast<const float4*>(sb + (xo ^ 16));
-                fma4(d0, x0, acc[s]);
-                fma4(d1, x1, acc[s]);
+                fma4(d0, *reinterpret_cast<const float4*>(sb + xo), acc[s]);
+                fma4(d1, *reinterpret_cast<const float4*>(sb + (xo ^ 16)), acc[s]);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[b]);  // this warp is done with stage b
@@ -403,24 +400,34 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
 // Returns -1 when the tiled path does not apply.
 int try_tiled(const sl_csr* W, const float* dY, const float* X, int64_t N, float* dW, cudaStream_t s) {
     const int64_t M = W->nrows, K = W->ncols;
-    if (N < 256 || N % kTJ != 0 || !aligned16(dY) || !aligned16(X) || N > INT_MAX / 2) return -1;
+    if (N < 1024 || N % kTJ != 0 || !aligned16(dY) || !aligned16(X) || N > INT_MAX / 2) return -1;
     // Live density estimate from the capacity (live + about 20% padding).
+    // Measured on B200 (standalone sweep): the tiled kernel wins for
+    // 2% <= density <= 40% once N >= 1024; at N = 256 its pipeline barely
+    // fills, and at 50% density its tiles shrink to 8 rows.
     const double dens = static_cast<double>(W->total_capacity) / 1.2 / (static_cast<double>(M) * K);
-    if (dens < 0.02) return -1;
-    int TR = static_cast<int>(std::floor(480.0 / (kTCols * dens) / 8.0)) * 8;
+    if (dens < 0.02 || dens > 0.4) return -1;
+    // Wide tiles at low density (more slots per tile row: fewer dY reloads),
+    // about 480 slots per tile (the batch holds 512).
+    int TC = dens <= 0.15 ? 128 : 64;
+    if (const char* e = std::getenv("SPARSECORE_B200_DW_TC")) {  // tuning knob: 64|128|256
+        const int v = std::atoi(e);
+        if (v == 64 || v == 128 || v == 256) TC = v;
+    }
+    int TR = static_cast<int>(std::floor(480.0 / (TC * dens) / 8.0)) * 8;
     TR = TR < 8 ? 8 : (TR > kTMaxRows ? kTMaxRows : TR);
-    const int TC = kTCols;
     unsigned* status = device_status_word();
     if (status == nullptr) return -1;
     CUtensorMap dymap, xmap;
     if (!make_tmap_2d(&dymap, dY, M, N, TR, kTJ, true) || !make_tmap_2d(&xmap, X, K, N, TC, kTJ, true))
         return -1;
     const size_t smem = static_cast<size_t>(kTStages * (TR + TC) * kTJ * 4) + 1024;
-    if (cudaFuncSetAttribute(sddmm_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    auto kern = sddmm_tiled_kernel;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
         return -1;
     const int n_bi = static_cast<int>((M + TR - 1) / TR), n_bc = static_cast<int>((K + TC - 1) / TC);
-    sddmm_tiled_kernel<<<n_bi * n_bc, kTThreads + 32, smem, s>>>(
+    kern<<<n_bi * n_bc, kTThreads + 32, smem, s>>>(
         dymap, xmap, static_cast<int>(M), N, TR, TC, n_bc, W->row_start, W->row_nnz,
         W->row_capacity, W->col_indices, dW, status);
     SL_RETURN_IF_LAUNCH_FAILED("sl_sddmm_dw (tiled)");

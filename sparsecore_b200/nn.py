@@ -18,7 +18,7 @@ import torch.nn as nn
 
 from . import _native as N
 from .layout import PaddedCSR, from_dense
-from .ops import _SpMMFunction
+from .ops import _SparseLinearFunction
 
 __all__ = ["SparseLinear"]
 
@@ -93,9 +93,7 @@ class SparseLinear(nn.Module):
             raise ValueError(f"SparseLinear expects input last dim {self.in_features}, "
                              f"got {orig_shape[-1]}")
         x_flat = x.reshape(-1, self.in_features)
-        X_col = x_flat.t().contiguous()
-        Y_col = _SpMMFunction.apply(self._values, self._csr, X_col, "simd")
-        y_flat = Y_col.t()
+        y_flat = _SparseLinearFunction.apply(self._values, self._csr, x_flat)
         if self.bias is not None:
             y_flat = y_flat + self.bias
         return y_flat.reshape(orig_shape[:-1] + (self.out_features,))

@@ -124,6 +124,16 @@ def _sddmm_raw(W: PaddedCSR, dY: torch.Tensor, X: torch.Tensor) -> torch.Tensor:
     return dW
 
 
+def _transpose(t: torch.Tensor) -> torch.Tensor:
+    """[r, c] fp32 CUDA tensor -> contiguous [c, r] copy (sl_transpose_f32)."""
+    t = t.to(dtype=torch.float32).contiguous()
+    r, c = t.shape
+    out = torch.empty(c, r, dtype=torch.float32, device=t.device)
+    _launch("transpose", 8 * r * c, 0,
+            lambda: N.call("sl_transpose_f32", N.ptr(t), r, c, N.ptr(out), N.stream_ptr(t.device)))
+    return out
+
+
 def _check_dense(W: PaddedCSR, X: torch.Tensor, fn: str) -> torch.Tensor:
     if X.device.type != "cuda":
         raise RuntimeError(f"{fn}: X must be on a CUDA device (got device={X.device}). "
@@ -168,6 +178,47 @@ class _SpMMFunction(torch.autograd.Function):
             WT = _cached_transpose(W)
             dX = _spmm_raw(WT, dY_c, kind="spmm_dx")
         return dW, None, dX, None
+
+
+class _SparseLinearFunction(torch.autograd.Function):
+    """Token-major form of ``_SpMMFunction`` used by ``SparseLinear``:
+    ``y[T, M] = x[T, K] . W^T`` for activations laid out [tokens, features].
+
+    The reference builds the kernels' column-per-token operand with torch
+    copies (``sparselab/nn.py:229-237``: ``x.reshape(-1, in).t().contiguous()``
+    and ``Y.t()`` of the result, leaving a strided output).  Here both
+    directions go through ``sl_transpose_f32`` and the output is returned
+    contiguous, so the surrounding element-wise ops stay vectorised:
+
+        forward:  X = x^T;  Y = W.X (sl_spmm_fwd);  y = Y^T
+        backward: dY = dy^T;  dW = SDDMM(dY, X);  dX = W^T.dY (cached
+                  transpose);  dx = dX^T
+
+    Transposes are exact copies, so every value equals ``_SpMMFunction``'s on
+    ``x.t()``.  Inputs ``(W_values, W, x)``; backward returns
+    ``(dW_values[total_capacity], None, dx)``.
+    """
+
+    @staticmethod
+    def forward(ctx, W_values, W, x):
+        if x.device.type != "cuda" or x.device != W.device:
+            raise RuntimeError(f"SparseLinear: input must be on {W.device} (got {x.device}); "
+                               f"sparsecore_b200 has no CPU path.")
+        X = _transpose(x)
+        ctx.save_for_backward(W_values, X)
+        ctx.W = W
+        return _transpose(_spmm_raw(W, X))
+
+    @staticmethod
+    def backward(ctx, dy):
+        W_values, X = ctx.saved_tensors
+        W = ctx.W
+        dY = _transpose(dy)
+        dW = _sddmm_raw(W, dY, X) if ctx.needs_input_grad[0] else None
+        dx = None
+        if ctx.needs_input_grad[2]:
+            dx = _transpose(_spmm_raw(_cached_transpose(W), dY, kind="spmm_dx"))
+        return dW, None, dx
 
 
 def spmm(W: PaddedCSR, X: torch.Tensor, *, kernel: str = "auto") -> torch.Tensor:

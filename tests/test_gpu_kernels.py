@@ -190,7 +190,8 @@ def test_forward_paths_and_sddmm_variants_vs_oracle(path, monkeypatch):
 
 
 @pytest.mark.parametrize("M,K,N,block", [(301, 517, 256, False), (700, 300, 512, True),
-                                         (96, 2000, 288, False), (1000, 1000, 320, True)])
+                                         (96, 2000, 288, False), (1000, 1000, 320, True),
+                                         (2100, 3100, 256, True)])
 def test_tiled_sddmm_matches_slot_kernels_and_oracle(M, K, N, block, monkeypatch):
     """The tiled SDDMM (large N) against the per-slot kernels and the oracle:
     edge tiles (M, K not multiples of the tile), and a dense block that puts
@@ -208,8 +209,14 @@ def test_tiled_sddmm_matches_slot_kernels_and_oracle(M, K, N, block, monkeypatch
     W = sl.PaddedCSR.from_dense(Wd.to(d))
     X = torch.randn(K, N, generator=g)
     dY = torch.randn(M, N, generator=g)
+    Wo = oracle_csr(W)
+    # forward on the same shapes: K > 1536 takes the K-blocked X-stationary kernel
+    assert bits_equal(sl.spmm(W, X.to(d)), O.spmm(Wo, X.numpy()))
+    WT, _ = sl.transpose_with_perm(W)
+    WTo, _ = O.transpose_with_perm(Wo)
+    assert bits_equal(ops._spmm_raw(WT, dY.to(d)), O.spmm(WTo, dY.numpy()))
     tiled = ops._sddmm_raw(W, dY.to(d), X.to(d))
     monkeypatch.setenv("SPARSECORE_B200_DW", "quad")
     per_slot = ops._sddmm_raw(W, dY.to(d), X.to(d))
     assert bits_equal(tiled, per_slot)
-    assert bits_equal(tiled, O.sddmm(oracle_csr(W), dY.numpy(), X.numpy()))
+    assert bits_equal(tiled, O.sddmm(Wo, dY.numpy(), X.numpy()))

@@ -166,3 +166,13 @@ def test_spmm_validation_errors():
         assert sl.spmm(W, torch.ones(6, 2, device=dev()), kernel=k).shape == (4, 2)
     # fp64 input is coerced to fp32
     assert sl.spmm(W, torch.ones(6, 2, device=dev(), dtype=torch.float64)).dtype == torch.float32
+
+
+def test_dense_transpose_kernel_exact():
+    """sl_transpose_f32 (SparseLinear's layout change) is an exact copy."""
+    from sparsecore_b200 import ops
+
+    g = torch.Generator().manual_seed(5)
+    for r, c in [(1, 1), (33, 65), (1000, 7), (7, 1000), (512, 3072)]:
+        a = torch.randn(r, c, generator=g).cuda()
+        assert torch.equal(ops._transpose(a), a.t().contiguous()), (r, c)
