@@ -17,8 +17,8 @@
 // coalesced loads (one row-run of CH slots per load instruction; rows padded
 // to CH+1 pairs so the groups' broadcast reads fall in different banks),
 // then each lane walks its own row's staged slots.  Work items (row group,
-// column tile) are ordered column-tile fastest so that warps resident
-// together share the same W segment (L1/L2 hits) and sweep X once.
+// column tile) are ordered row-group fastest, so that the warps resident
+// together work on one band of column tiles whose X slice stays in L2.
 #include <cstdlib>
 #include <cstring>
 
@@ -123,8 +123,12 @@ spmm_fwd_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
 
     for (int64_t item = static_cast<int64_t>(blockIdx.x) * warps_per_block + warp; item < n_items;
          item += static_cast<int64_t>(gridDim.x) * warps_per_block) {
-        const int64_t nt = item % n_tiles;
-        const int row = static_cast<int>(item / n_tiles) * RPW + g;
+        // Row groups fastest: the warps resident together share one band of
+        // column tiles, whose X slice stays in L2 (W is small and stays in
+        // L2 across bands).
+        const int64_t n_groups = (M + RPW - 1) / RPW;
+        const int64_t nt = item / n_groups;
+        const int row = static_cast<int>(item % n_groups) * RPW + g;
         const bool valid = row < M;
         int rs = 0, nn = 0;
         if (valid) {
