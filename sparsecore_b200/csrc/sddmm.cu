@@ -22,7 +22,7 @@
 //    contiguous 64-byte piece of the X row per step; each quad carries S = 4
 //    slots of the row, reusing each dY vector 4 times.
 //  * N < 16 (lane kernel): each lane evaluates one slot's whole dot
-//    (segments of 128 slots, so 4 slots per lane are in flight).
+//    (segments of 128 slots, 4 per lane).
 #include <cmath>
 #include <cstdlib>
 
@@ -158,12 +158,28 @@ sddmm_quad_kernel(int M, int spr, int64_t N, const int32_t* __restrict__ row_sta
     }
 }
 
-// One slot's whole dot (N < 16: no 16-wide steps, so all 16 chains are +0
-// before the optional 8-wide step).
+// One slot's whole dot for small N: the 16 chains in registers (16-wide
+// steps as four 128-bit loads of each operand when VEC4), then the same
+// combination, optional 8-wide step, horizontal reduction and tail.
+template <bool VEC4>
 __device__ __forceinline__ float lane_dot(const float* dyr, const float* xr, const DwShape& sh) {
-    float a[8];
+    float a[16];
 #pragma unroll
-    for (int t = 0; t < 8; ++t) a[t] = __fadd_rn(0.0f, 0.0f);
+    for (int t = 0; t < 16; ++t) a[t] = 0.0f;
+    for (int64_t m = 0; m < sh.nfull; ++m) {
+        const float* d = dyr + m * 16;
+        const float* x = xr + m * 16;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            const float4 dv = load4<VEC4>(d + 4 * h), xv = load4<VEC4>(x + 4 * h);
+            a[4 * h + 0] = fmaf(dv.x, xv.x, a[4 * h + 0]);
+            a[4 * h + 1] = fmaf(dv.y, xv.y, a[4 * h + 1]);
+            a[4 * h + 2] = fmaf(dv.z, xv.z, a[4 * h + 2]);
+            a[4 * h + 3] = fmaf(dv.w, xv.w, a[4 * h + 3]);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < 8; ++t) a[t] = __fadd_rn(a[t], a[t + 8]);
     if (sh.rem >= 8)
 #pragma unroll
         for (int t = 0; t < 8; ++t)
@@ -175,9 +191,10 @@ __device__ __forceinline__ float lane_dot(const float* dyr, const float* xr, con
     return dot_tail(r, dyr, xr, sh.jtail, sh.jfma, sh.N);
 }
 
-// N < 16: one lane per slot (segments of 128 slots, 4 per lane in flight),
-// all chains in registers.
+// Small N: one lane per slot (segments of 128 slots, 4 per lane), all
+// chains in registers.
 constexpr int kLaneSeg = 128;
+template <bool VEC4>
 __global__ void __launch_bounds__(kDwThreads)
 sddmm_lane_kernel(int M, int spr, int64_t N, const int32_t* __restrict__ row_start,
                   const int32_t* __restrict__ row_nnz, const int32_t* __restrict__ row_capacity,
@@ -205,7 +222,7 @@ sddmm_lane_kernel(int M, int spr, int64_t N, const int32_t* __restrict__ row_sta
             }
             float r[U];
 #pragma unroll
-            for (int u = 0; u < U; ++u) r[u] = lane_dot(dyr, xr[u], sh);
+            for (int u = 0; u < U; ++u) r[u] = lane_dot<VEC4>(dyr, xr[u], sh);
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int k = kb + u * 32 + lane;
@@ -443,7 +460,9 @@ bool tiled_disabled() {
 int launch_dw(const sl_csr* W, const float* dY, const float* X, int64_t N, float* dW,
               cudaStream_t s) {
     const int M = static_cast<int>(W->nrows);
-    const bool lane_kernel = N < 16;
+    int64_t lane_max = 16;  // lane kernel below this N (tuning knob: SPARSECORE_B200_DW_LANE)
+    if (const char* e = std::getenv("SPARSECORE_B200_DW_LANE")) lane_max = std::atoi(e);
+    const bool lane_kernel = N < lane_max;
     const int seg = lane_kernel ? kLaneSeg : kSeg;
     const int64_t avg_cap = (W->total_capacity + M - 1) / M;
     const int spr = static_cast<int>(avg_cap > seg ? (avg_cap + seg - 1) / seg : 1);
@@ -453,8 +472,12 @@ int launch_dw(const sl_csr* W, const float* dY, const float* X, int64_t N, float
     if (blocks > max_blocks) blocks = max_blocks;
     const bool vec4 = (N % 4 == 0) && aligned16(X) && aligned16(dY);
     if (lane_kernel) {
-        sddmm_lane_kernel<<<static_cast<unsigned>(blocks), kDwThreads, 0, s>>>(
-            M, spr, N, W->row_start, W->row_nnz, W->row_capacity, W->col_indices, dY, X, dW);
+        if (vec4)
+            sddmm_lane_kernel<true><<<static_cast<unsigned>(blocks), kDwThreads, 0, s>>>(
+                M, spr, N, W->row_start, W->row_nnz, W->row_capacity, W->col_indices, dY, X, dW);
+        else
+            sddmm_lane_kernel<false><<<static_cast<unsigned>(blocks), kDwThreads, 0, s>>>(
+                M, spr, N, W->row_start, W->row_nnz, W->row_capacity, W->col_indices, dY, X, dW);
     } else if (vec4) {
         sddmm_quad_kernel<true><<<static_cast<unsigned>(blocks), kDwThreads, 0, s>>>(
             M, spr, N, W->row_start, W->row_nnz, W->row_capacity, W->col_indices, dY, X, dW);

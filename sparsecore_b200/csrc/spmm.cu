@@ -190,25 +190,32 @@ spmm_fwd_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
 
 // ── Small N: one row per warp ───────────────────────────────────────────
 // For N < 128 a row's work is short, so rows (not columns) must supply the
-// parallelism: each warp owns one row at a time (M warps in flight).  Per
-// chunk of 32 slots every lane loads one (col, value) pair (coalesced; the
-// next chunk's pair is loaded while the current chunk is consumed) and puts
-// it in the warp's shared-memory slot buffer; the warp then walks the chunk
-// in slot order with broadcast reads; lane j accumulates columns j, j+32,
-// ... (CPL of them).  With N = 1 each lane also gathers X[col] of its own
-// pair up front and the buffer holds (value, x) pairs, read two slots per
-// 128-bit load, so the chain costs half a shared load and one FMA per slot.
-// Same FMA chain per element as above.
-template <int CPL, bool N1>
+// parallelism: each warp owns one row at a time (M warps in flight).  The
+// row is consumed in chunks of 32 slots: every lane holds one (col, value)
+// pair of a chunk, and the pairs of the next three chunks are already in
+// flight in a four-entry register ring (a chunk's chain is short, so the
+// loads need that distance to cover HBM latency).  A chunk's pairs go to the
+// warp's shared-memory buffer and the warp walks them in slot order, two
+// pairs per 128-bit broadcast read; lane j accumulates columns j, j+32, ...
+// (CPL of them).  With N = 1 each lane gathers X[col] of its pair one chunk
+// ahead and the buffer holds (value, x), so the chain costs half a shared
+// load and one FMA per slot.  Same FMA chain per element as above.
+template <int CPL, bool N1, bool FULL>
 __global__ void __launch_bounds__(256)
 spmm_rowwarp_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
                     const int32_t* __restrict__ row_nnz, const int32_t* __restrict__ cols,
                     const float* __restrict__ vals, const float* __restrict__ X,
                     float* __restrict__ Y) {
+    constexpr int R = 4;  // register ring of chunk pairs
     __shared__ __align__(16) int2 buf[8][32];
     const int lane = threadIdx.x & 31;
     int2* st = buf[threadIdx.x >> 5];
-    const float4* st4 = reinterpret_cast<const float4*>(st);
+    const int4* st4 = reinterpret_cast<const int4*>(st);
+    // Columns past N (FULL = false) read a valid clamped address; their
+    // accumulators are never stored, so the loads need no predicate.
+    int jcol[CPL];
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) jcol[k] = FULL ? lane + 32 * k : min(lane + 32 * k, static_cast<int>(N) - 1);
     const int warps = gridDim.x * (blockDim.x >> 5);
     for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < M; row += warps) {
         const int rs = __ldg(row_start + row);
@@ -216,52 +223,70 @@ spmm_rowwarp_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
         float acc[CPL];
 #pragma unroll
         for (int cc = 0; cc < CPL; ++cc) acc[cc] = 0.0f;
-        int c = 0;
-        float v = 0.0f;
-        if (lane < nn) {
-            c = __ldg(cols + rs + lane);
-            v = __ldg(vals + rs + lane);
-        }
-        for (int base = 0; base < nn; base += 32) {
-            if constexpr (N1) {
-                const float x = base + lane < nn ? __ldg(X + c) : 0.0f;
-                st[lane] = make_int2(__float_as_int(v), __float_as_int(x));
-            } else {
-                st[lane] = make_int2(c, __float_as_int(v));
-            }
-            const int nk = base + 32 + lane;  // next chunk's pair in flight
-            if (nk < nn) {
-                c = __ldg(cols + rs + nk);
-                v = __ldg(vals + rs + nk);
-            }
-            __syncwarp();
-            const int cnt = min(32, nn - base);
-            if constexpr (N1) {
-                int t = 0;
-#pragma unroll 8
-                for (; t + 1 < cnt; t += 2) {
-                    const float4 q = st4[t >> 1];
-                    acc[0] = fmaf(q.x, q.y, acc[0]);
-                    acc[0] = fmaf(q.z, q.w, acc[0]);
-                }
-                if (t < cnt) {
-                    const int2 e = st[t];
-                    acc[0] = fmaf(__int_as_float(e.x), __int_as_float(e.y), acc[0]);
-                }
-            } else {
-#pragma unroll 16
-                for (int t = 0; t < cnt; ++t) {
-                    const int2 e = st[t];
-                    const float vt = __int_as_float(e.y);
-                    const float* xr = X + static_cast<int64_t>(e.x) * N;
+        int cr[R];
+        float vr[R];
 #pragma unroll
-                    for (int k = 0; k < CPL; ++k) {
-                        const int64_t j = lane + 32 * k;
-                        if (j < N) acc[k] = fmaf(vt, __ldg(xr + j), acc[k]);
+        for (int j = 0; j < R; ++j) {
+            const int k = 32 * j + lane;
+            cr[j] = k < nn ? __ldg(cols + rs + k) : 0;
+            vr[j] = k < nn ? __ldg(vals + rs + k) : 0.0f;
+        }
+        float xn = 0.0f;
+        if constexpr (N1) xn = lane < nn ? __ldg(X + cr[0]) : 0.0f;
+        for (int base = 0; base < nn; base += 32 * R) {
+#pragma unroll
+            for (int j = 0; j < R; ++j) {
+                const int b = base + 32 * j;
+                if (b >= nn) break;
+                if constexpr (N1) {
+                    st[lane] = make_int2(__float_as_int(vr[j]), __float_as_int(xn));
+                    xn = b + 32 + lane < nn ? __ldg(X + cr[(j + 1) % R]) : 0.0f;  // next chunk's gather
+                } else {
+                    st[lane] = make_int2(cr[j], __float_as_int(vr[j]));
+                }
+                const int k = b + 32 * R + lane;  // refill: chunk b + 32R
+                if (k < nn) {
+                    cr[j] = __ldg(cols + rs + k);
+                    vr[j] = __ldg(vals + rs + k);
+                }
+                __syncwarp();
+                const int cnt = min(32, nn - b);
+                int t = 0;
+                if constexpr (N1) {
+#pragma unroll 8
+                    for (; t + 1 < cnt; t += 2) {
+                        const float4 q = reinterpret_cast<const float4*>(st4)[t >> 1];
+                        acc[0] = fmaf(q.x, q.y, acc[0]);
+                        acc[0] = fmaf(q.z, q.w, acc[0]);
+                    }
+                    if (t < cnt) {
+                        const int2 e = st[t];
+                        acc[0] = fmaf(__int_as_float(e.x), __int_as_float(e.y), acc[0]);
+                    }
+                } else {
+                    constexpr int kUnroll = CPL >= 3 ? 4 : 8;
+#pragma unroll kUnroll
+                    for (; t + 1 < cnt; t += 2) {
+                        const int4 e = st4[t >> 1];
+                        const float* x0 = X + static_cast<int64_t>(e.x) * N;
+                        const float* x1 = X + static_cast<int64_t>(e.z) * N;
+#pragma unroll
+                        for (int q = 0; q < CPL; ++q) {
+                            const float a0 = __ldg(x0 + jcol[q]), a1 = __ldg(x1 + jcol[q]);
+                            acc[q] = fmaf(__int_as_float(e.y), a0, acc[q]);
+                            acc[q] = fmaf(__int_as_float(e.w), a1, acc[q]);
+                        }
+                    }
+                    if (t < cnt) {
+                        const int2 e = st[t];
+                        const float* x0 = X + static_cast<int64_t>(e.x) * N;
+#pragma unroll
+                        for (int q = 0; q < CPL; ++q)
+                            acc[q] = fmaf(__int_as_float(e.y), __ldg(x0 + jcol[q]), acc[q]);
                     }
                 }
+                __syncwarp();
             }
-            __syncwarp();
         }
         float* yr = Y + static_cast<int64_t>(row) * N;
 #pragma unroll
@@ -272,13 +297,13 @@ spmm_rowwarp_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
     }
 }
 
-template <int CPL, bool N1>
+template <int CPL, bool N1, bool FULL = false>
 int launch_rowwarp(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_t s) {
     const int M = static_cast<int>(W->nrows);
     int64_t blocks = (static_cast<int64_t>(M) + 7) / 8;
     const int64_t max_blocks = static_cast<int64_t>(num_sms()) * 8;
     if (blocks > max_blocks) blocks = max_blocks;
-    spmm_rowwarp_kernel<CPL, N1><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+    spmm_rowwarp_kernel<CPL, N1, FULL><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
         M, N, W->row_start, W->row_nnz, W->col_indices, W->values, X, Y);
     SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd");
     return SL_OK;
@@ -286,6 +311,9 @@ int launch_rowwarp(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStr
 
 int dispatch_rowwarp(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_t s) {
     if (N == 1) return launch_rowwarp<1, true>(W, X, N, Y, s);
+    if (N == 32) return launch_rowwarp<1, false, true>(W, X, N, Y, s);
+    if (N == 64) return launch_rowwarp<2, false, true>(W, X, N, Y, s);
+    if (N == 96) return launch_rowwarp<3, false, true>(W, X, N, Y, s);
     if (N <= 32) return launch_rowwarp<1, false>(W, X, N, Y, s);
     if (N <= 64) return launch_rowwarp<2, false>(W, X, N, Y, s);
     if (N <= 96) return launch_rowwarp<3, false>(W, X, N, Y, s);
