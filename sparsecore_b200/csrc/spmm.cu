@@ -253,6 +253,19 @@ spmm_rowwarp_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
                 const int cnt = min(32, nn - b);
                 int t = 0;
                 if constexpr (N1) {
+                    if (cnt == 32) {
+                        // Full chunk: every shared read first, then the chain
+                        // (one load latency per chunk on the critical path).
+                        float4 q[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) q[i] = reinterpret_cast<const float4*>(st4)[i];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            acc[0] = fmaf(q[i].x, q[i].y, acc[0]);
+                            acc[0] = fmaf(q[i].z, q[i].w, acc[0]);
+                        }
+                        t = 32;
+                    }
 #pragma unroll 8
                     for (; t + 1 < cnt; t += 2) {
                         const float4 q = reinterpret_cast<const float4*>(st4)[t >> 1];
@@ -264,6 +277,33 @@ spmm_rowwarp_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
                         acc[0] = fmaf(__int_as_float(e.x), __int_as_float(e.y), acc[0]);
                     }
                 } else {
+                    if (cnt == 32) {
+                        // Full chunk, in groups of G pairs: the group's shared
+                        // reads, then its X loads, then its FMAs.
+                        constexpr int G = CPL >= 3 ? 2 : 4;  // int4 = two slots each
+#pragma unroll
+                        for (int h = 0; h < 16; h += G) {
+                            int4 e[G];
+#pragma unroll
+                            for (int i = 0; i < G; ++i) e[i] = st4[h + i];
+                            float xa[G][CPL], xb[G][CPL];
+#pragma unroll
+                            for (int i = 0; i < G; ++i)
+#pragma unroll
+                                for (int q = 0; q < CPL; ++q) {
+                                    xa[i][q] = __ldg(X + static_cast<int64_t>(e[i].x) * N + jcol[q]);
+                                    xb[i][q] = __ldg(X + static_cast<int64_t>(e[i].z) * N + jcol[q]);
+                                }
+#pragma unroll
+                            for (int i = 0; i < G; ++i)
+#pragma unroll
+                                for (int q = 0; q < CPL; ++q) {
+                                    acc[q] = fmaf(__int_as_float(e[i].y), xa[i][q], acc[q]);
+                                    acc[q] = fmaf(__int_as_float(e[i].w), xb[i][q], acc[q]);
+                                }
+                        }
+                        t = 32;
+                    }
                     constexpr int kUnroll = CPL >= 3 ? 4 : 8;
 #pragma unroll kUnroll
                     for (; t + 1 < cnt; t += 2) {
