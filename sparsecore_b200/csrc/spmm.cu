@@ -280,7 +280,7 @@ spmm_rowwarp_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
                     if (cnt == 32) {
                         // Full chunk, in groups of G pairs: the group's shared
                         // reads, then its X loads, then its FMAs.
-                        constexpr int G = CPL >= 3 ? 2 : 4;  // int4 = two slots each
+                        constexpr int G = CPL == 1 ? 8 : (CPL == 2 ? 4 : 2);  // int4 = two slots
 #pragma unroll
                         for (int h = 0; h < 16; h += G) {
                             int4 e[G];
