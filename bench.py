@@ -40,6 +40,8 @@ def parse():
     ap.add_argument("--kernel", default=None,
                     help="profiling mode: SHAPE:KIND:N runs 2 launches of one kernel "
                          "(SHAPE in %s or MxK@sparsity; KIND fwd|dw|dx|transpose)" % list(SHAPES))
+    ap.add_argument("--workload", choices=["cfg5", "cfg4", "cfg2"], default="cfg5",
+                    help="training workload (default cfg5, the headline configuration)")
     ap.add_argument("--sweep", action="store_true",
                     help="config-3 standalone SpMM sweep: one JSON line per cell")
     return ap.parse_args()
@@ -179,19 +181,73 @@ def peaks():
         return FALLBACK_HBM_GBS, "fallback", 1965.0
 
 
-def workload_config(cfg, world):
-    return {
-        "workload": (f"{cfg.name}: d_model {cfg.d_model}, {cfg.n_layers} layers, {cfg.n_heads} "
-                     f"heads, ctx {cfg.seq_len}, vocab {cfg.vocab}, FFN {cfg.d_ff} at "
-                     f"{int(cfg.ffn_sparsity * 100)}% / attention projections at "
-                     f"{int(cfg.attn_sparsity * 100)}% sparsity (padded CSR, fp32), AdamW "
-                     f"{cfg.lr}, {cfg.router} every {cfg.update_freq} steps"),
-        "global_batch": cfg.batch * world,
-        "seq_len": cfg.seq_len,
-        "tokens_per_step": cfg.batch * cfg.seq_len * world,
-        "parallelism": f"dp{world}",
-        "l2": "inputs larger than L2 (per-step activations ~GBs, no flush needed)",
-    }
+def workload_config(wl, world):
+    cfg = dict(wl.config)
+    cfg["global_batch"] = cfg["global_batch"] * world
+    cfg["units_per_step"] = wl.units * world
+    cfg["parallelism"] = f"dp{world}"
+    cfg["l2"] = "inputs larger than L2 (per-step activations ~GBs, no flush needed)"
+    return cfg
+
+
+# ───────────────────────────── workloads ─────────────────────────────
+
+class Workload:
+    """One training configuration: model, router, optimizer, a synthetic batch
+    (on the host) and its loss.  `linear` builds the sparse projections (the
+    library's SparseLinear on a GPU, the reference kernels on the CPU)."""
+
+    def __init__(self, name, device, rank, linear=None, batch=None):
+        import sparsecore_b200 as sl
+        from sparsecore_b200 import workloads as W
+
+        self.name = name
+        dev = torch.device(device)
+        torch.manual_seed(0)  # identical replicas on every rank
+        if name in ("cfg5", "cfg4"):
+            cfg = W.CFG5 if name == "cfg5" else W.CFG4
+            self.cfg = cfg
+            self.model = W.MiniGPT(cfg, device=dev, linear=linear)
+            algo_cls = sl.SET if cfg.router == "SET" else sl.RigL
+            self.algo = algo_cls(sparsity=cfg.ffn_sparsity, drop_fraction=cfg.drop_fraction,
+                                 update_freq=cfg.update_freq, seed=0)
+            self.opt = torch.optim.AdamW(self.model.parameters(), lr=cfg.lr)
+            nb = batch or cfg.batch
+            self.batch = (W.synthetic_tokens(cfg, nb, seed=1000 + rank),)
+            self.units = nb * cfg.seq_len
+            self.unit = "tokens/s"
+            self.data = "synthetic (uniform random token ids)"
+            self.loss_fn = lambda m, b: W.lm_loss(m, b[0])
+            self.config = {
+                "workload": (f"{cfg.name}: d_model {cfg.d_model}, {cfg.n_layers} layers, "
+                             f"{cfg.n_heads} heads, ctx {cfg.seq_len}, vocab {cfg.vocab}, FFN "
+                             f"{cfg.d_ff} at {int(cfg.ffn_sparsity * 100)}% / attention "
+                             f"projections at {int(cfg.attn_sparsity * 100)}% sparsity (padded "
+                             f"CSR, fp32), AdamW {cfg.lr}, {cfg.router} every {cfg.update_freq} "
+                             f"steps"),
+                "global_batch": cfg.batch, "seq_len": cfg.seq_len}
+        else:  # cfg2: MLP 784 -> 512 -> 10, SGD 0.1, SET every 100 steps
+            make = linear or (lambda fin, fout, s, bias=True: sl.SparseLinear(fin, fout, bias=bias,
+                                                                              sparsity=s, device=dev))
+            self.model = torch.nn.Sequential(make(784, 512, 0.9, bias=True), torch.nn.ReLU(),
+                                             make(512, 10, 0.9, bias=True))
+            self.algo = sl.SET(sparsity=0.9, drop_fraction=0.3, update_freq=100, seed=0)
+            self.opt = torch.optim.SGD(self.model.parameters(), lr=0.1)
+            nb = batch or 256
+            g = torch.Generator().manual_seed(1000 + rank)
+            self.batch = (torch.randn(nb, 784, generator=g), torch.randint(0, 10, (nb,), generator=g))
+            self.units = nb
+            self.unit = "samples/s"
+            self.data = "synthetic (x ~ N(0,1), uniform int64 labels)"
+            self.loss_fn = lambda m, b: torch.nn.functional.cross_entropy(m(b[0]), b[1])
+            self.config = {"workload": "cfg2-mlp: 784->512->10 ReLU, both SparseLinear at 90%, "
+                                       "SGD 0.1, SET every 100 steps (drop 0.3)",
+                           "global_batch": 256, "seq_len": 1}
+        if linear is None:
+            self.model.apply(self.algo)
+
+    def h2d_bytes(self):
+        return sum(t.numel() * t.element_size() for t in self.batch)
 
 
 # ───────────────────────────── clocks ─────────────────────────────
@@ -241,28 +297,22 @@ class Clocks:
 # ───────────────────────────── our arm ─────────────────────────────
 
 def run_ours(args, rank, world, local_rank):
-    import sparsecore_b200 as sl
     from sparsecore_b200 import _native as N
     from sparsecore_b200 import ops
     from sparsecore_b200.dist import SparseDataParallel, sync_after_router_step
-    from sparsecore_b200.workloads import CFG5, MiniGPT, lm_loss, sparse_live_weights, synthetic_tokens
+    from sparsecore_b200.workloads import sparse_live_weights
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    cfg = CFG5
-    torch.manual_seed(0)  # identical replicas on every rank
-    model = MiniGPT(cfg, device=dev)
-    algo = sl.SET(sparsity=cfg.ffn_sparsity, drop_fraction=cfg.drop_fraction,
-                  update_freq=cfg.update_freq, seed=0)
-    model.apply(algo)
-    opt = torch.optim.AdamW(model.parameters(), lr=cfg.lr)
+    wl = Workload(args.workload, dev, rank)
+    model, algo, opt = wl.model, wl.algo, wl.opt
     ddp = SparseDataParallel(model)
-    tokens_host = synthetic_tokens(cfg, cfg.batch, seed=1000 + rank).pin_memory()
-    tokens_dev = tokens_host.to(dev)
+    batch_host = tuple(t.pin_memory() for t in wl.batch)
+    batch_dev = tuple(t.to(dev) for t in batch_host)
 
-    def step(tok):
+    def step(batch):
         opt.zero_grad(set_to_none=True)
-        loss = lm_loss(model, tok)
+        loss = wl.loss_fn(model, batch)
         loss.backward()
         ddp.allreduce_grads()
         opt.step()
@@ -276,7 +326,7 @@ def run_ours(args, rank, world, local_rank):
             dist.barrier()
 
     for _ in range(args.warmup):
-        step(tokens_dev)
+        step(batch_dev)
     barrier()
 
     timer = ops.KernelTimer()
@@ -289,7 +339,7 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     e0.record(s)
     for _ in range(args.steps):
-        step(tokens_dev)
+        step(batch_dev)
     e1.record(s)
     barrier()
     launches = N.launches["count"] - l0
@@ -302,8 +352,8 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     w0 = time.perf_counter()
     for _ in range(args.steps):
-        tok = tokens_host.to(dev, non_blocking=True)
-        float(step(tok).item())
+        b = tuple(t.to(dev, non_blocking=True) for t in batch_host)
+        float(step(b).item())
     barrier()
     e2e_ms = (time.perf_counter() - w0) * 1e3
 
@@ -322,7 +372,7 @@ def run_ours(args, rank, world, local_rank):
     if rank != 0:
         return None
 
-    tokens = cfg.batch * cfg.seq_len * world * args.steps
+    tokens = wl.units * world * args.steps
     hbm, hbm_src, sm_max = peaks()
     dom = max(ksum, key=lambda k: ksum[k]["ms"]) if ksum else None
     roof = None
@@ -344,24 +394,27 @@ def run_ours(args, rank, world, local_rank):
                             for k, v in ksum.items()},
                 "step_share": round(sum(v["ms"] for v in ksum.values()) / t_ms, 3)}
     line = {
-        "metric": METRIC, "value": round(tokens / (t_ms * 1e-3), 1), "unit": "tokens/s",
+        "metric": METRIC, "value": round(tokens / (t_ms * 1e-3), 1), "unit": wl.unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(t_ms / args.steps, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (uniform random byte tokens)",
-        "config": dict(workload_config(cfg, world), sparse_live_weights=sparse_live_weights(model)),
+        "vs_baseline": None, "dtype": "f32", "data": wl.data,
+        "config": dict(workload_config(wl, world), sparse_live_weights=sparse_live_weights(model)),
         "roofline": roof,
-        "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": tokens_host.numel() * tokens_host.element_size(),
+        "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": wl.unit,
+                "h2d_bytes_per_step": wl.h2d_bytes(),
                 "d2h_bytes_per_step": 4},
         "gpu_launches": launches,
         "clocks": clk,
-        "router": {"algorithm": "SET", "every_steps": cfg.update_freq,
+        "router": {"algorithm": type(algo).__name__, "every_steps": algo.update_freq,
                    "update_plus_broadcast_ms": round(router_ms, 1),
                    "note": "no update falls inside the timed window; amortised cost per step = "
                            "update_plus_broadcast_ms / every_steps"},
     }
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_sample(cfg, args.cpu_seqs, 1, 2)
+        cb = cpu_sample(args.workload, args.cpu_seqs, 1, 2)
+        cb.pop("_config")
+        cb.pop("_data")
+        line["cpu_baseline"] = cb
     return line
 
 
@@ -380,23 +433,25 @@ def read_traffic(kernel):
 
 # ───────────────────────────── reference arm ─────────────────────────────
 
-def cpu_sample(cfg, seqs, warmup, steps):
-    """The reference's CPU implementation of the path on a bounded sample."""
+def cpu_sample(workload, seqs, warmup, steps):
+    """The reference's CPU implementation of the path on a bounded sample:
+    the same model with every sparse projection on the reference's own
+    compiled kernels (OpenMP, all host threads) and stock torch CPU ops for
+    the dense parts; `seqs` sequences per step (cfg4/cfg5) or the full
+    256-sample batch (cfg2, cheap on the CPU)."""
     threads = os.cpu_count() or 1
     os.environ.setdefault("OMP_NUM_THREADS", str(threads))
     torch.set_num_threads(threads)
     from oracle import ref_arm
-    from sparsecore_b200.workloads import MiniGPT, lm_loss, synthetic_tokens
 
     kern = ref_arm.kernels()
-    torch.manual_seed(0)
-    model = MiniGPT(cfg, device="cpu", linear=ref_arm.linear_factory(kern))
-    opt = torch.optim.AdamW(model.parameters(), lr=cfg.lr)
-    tok = synthetic_tokens(cfg, seqs, seed=1000)
+    wl = Workload(workload, "cpu", 0, linear=ref_arm.linear_factory(kern),
+                  batch=seqs if workload != "cfg2" else None)
+    model, opt = wl.model, wl.opt
 
     def step():
         opt.zero_grad(set_to_none=True)
-        loss = lm_loss(model, tok)
+        loss = wl.loss_fn(model, wl.batch)
         loss.backward()
         opt.step()
         return float(loss.item())
@@ -407,27 +462,30 @@ def cpu_sample(cfg, seqs, warmup, steps):
     for _ in range(steps):
         step()
     dt = time.perf_counter() - t0
-    return {"value": round(seqs * cfg.seq_len * steps / dt, 2), "unit": "tokens/s",
+    return {"value": round(wl.units * steps / dt, 2), "unit": wl.unit,
+            "_config": wl.config, "_data": wl.data,
             "cores": threads if kern.kind == "reference" else 1, "kind": kern.kind,
-            "sample": f"{steps} training steps of {seqs} x {cfg.seq_len} tokens (config-5 model, "
-                      f"{warmup} warm-up), reference _core kernels (OpenMP) + torch CPU dense ops",
+            "sample": f"{steps} training steps of {wl.units} {wl.unit.split('/')[0]} ({workload} "
+                      f"model, {warmup} warm-up), reference _core kernels (OpenMP) + torch CPU "
+                      f"dense ops",
             "ms_per_step": round(dt / steps * 1e3, 1)}
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return None
-    from sparsecore_b200.workloads import CFG5
-
-    cfg = CFG5
-    cb = cpu_sample(cfg, args.cpu_seqs, max(1, min(args.warmup, 2)), max(1, min(args.steps, 5)))
+    cb = cpu_sample(args.workload, args.cpu_seqs, max(1, min(args.warmup, 2)),
+                    max(1, min(args.steps, 5)))
+    ref = {"config": cb.pop("_config"), "data": cb.pop("_data")}
     return {
-        "metric": METRIC, "impl": "reference", "value": cb["value"], "unit": "tokens/s",
+        "metric": METRIC, "impl": "reference", "value": cb["value"], "unit": cb["unit"],
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": cb["ms_per_step"], "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (uniform random byte tokens)",
-        "config": workload_config(cfg, world), "cpu_baseline": cb,
-        "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+        "vs_baseline": None, "dtype": "f32", "data": ref["data"],
+        "config": dict(ref["config"], global_batch=ref["config"]["global_batch"] * world,
+                       parallelism=f"dp{world}"),
+        "cpu_baseline": cb,
+        "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
 

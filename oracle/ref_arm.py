@@ -112,6 +112,8 @@ class RefSparseLinear(nn.Module):
     reference (sparselab/nn.py:118-185)."""
 
     def __init__(self, fin, fout, sparsity, kern, bias=False, padding_ratio=0.2):
+        """bias=True adds the reference's bias (uniform +-1/sqrt(fan), drawn
+        after the weights, sparselab/nn.py:113-116)."""
         super().__init__()
         self.in_features, self.out_features = fin, fout
         self.kernels = kern
@@ -124,7 +126,7 @@ class RefSparseLinear(nn.Module):
         self._p = p
         self.W = kern.make(p)
         self._values = nn.Parameter(torch.from_numpy(kern.values(self.W)))
-        self.bias = None
+        self.bias = nn.Parameter(torch.empty(fout).uniform_(-bound, bound)) if bias else None
         self._wt = None
 
     def cached_transpose(self):
@@ -142,10 +144,12 @@ class RefSparseLinear(nn.Module):
         shp = x.shape
         X_col = x.reshape(-1, self.in_features).t().contiguous()
         y = _RefSpMM.apply(self._values, self, X_col).t()
+        if self.bias is not None:
+            y = y + self.bias
         return y.reshape(shp[:-1] + (self.out_features,))
 
 
 def linear_factory(kern):
-    def make(fin, fout, sparsity):
-        return RefSparseLinear(fin, fout, sparsity, kern)
+    def make(fin, fout, sparsity, bias=False):
+        return RefSparseLinear(fin, fout, sparsity, kern, bias=bias)
     return make
