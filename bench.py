@@ -42,6 +42,9 @@ def parse():
                          "(SHAPE in %s or MxK@sparsity; KIND fwd|dw|dx|transpose)" % list(SHAPES))
     ap.add_argument("--workload", choices=["cfg5", "cfg4", "cfg2"], default="cfg5",
                     help="training workload (default cfg5, the headline configuration)")
+    ap.add_argument("--graph", action="store_true",
+                    help="replay the training step as a CUDA graph (re-captured after "
+                         "topology updates); per-kernel timings then come from an eager pass")
     ap.add_argument("--sweep", action="store_true",
                     help="config-3 standalone SpMM sweep: one JSON line per cell")
     return ap.parse_args()
@@ -197,7 +200,7 @@ class Workload:
     (on the host) and its loss.  `linear` builds the sparse projections (the
     library's SparseLinear on a GPU, the reference kernels on the CPU)."""
 
-    def __init__(self, name, device, rank, linear=None, batch=None):
+    def __init__(self, name, device, rank, linear=None, batch=None, capturable=False):
         import sparsecore_b200 as sl
         from sparsecore_b200 import workloads as W
 
@@ -211,7 +214,8 @@ class Workload:
             algo_cls = sl.SET if cfg.router == "SET" else sl.RigL
             self.algo = algo_cls(sparsity=cfg.ffn_sparsity, drop_fraction=cfg.drop_fraction,
                                  update_freq=cfg.update_freq, seed=0)
-            self.opt = torch.optim.AdamW(self.model.parameters(), lr=cfg.lr)
+            self.opt = torch.optim.AdamW(self.model.parameters(), lr=cfg.lr,
+                                         capturable=capturable)
             nb = batch or cfg.batch
             self.batch = (W.synthetic_tokens(cfg, nb, seed=1000 + rank),)
             self.units = nb * cfg.seq_len
@@ -304,33 +308,55 @@ def run_ours(args, rank, world, local_rank):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    wl = Workload(args.workload, dev, rank)
+    wl = Workload(args.workload, dev, rank, capturable=args.graph)
     model, algo, opt = wl.model, wl.algo, wl.opt
     ddp = SparseDataParallel(model)
     batch_host = tuple(t.pin_memory() for t in wl.batch)
     batch_dev = tuple(t.to(dev) for t in batch_host)
 
-    def step(batch):
+    def train(*batch):
         opt.zero_grad(set_to_none=True)
         loss = wl.loss_fn(model, batch)
         loss.backward()
         ddp.allreduce_grads()
         opt.step()
+        return loss
+
+    def route():
         algo.step()
         sync_after_router_step(ddp, algo)
+
+    def step(batch):
+        loss = train(*batch)
+        route()
         return loss
+
+    graphed = None
+    if args.graph:
+        from sparsecore_b200.graph import GraphedStep
+
+        graphed = GraphedStep(model, train, batch_dev)
+
+        def step(batch):  # noqa: F811 - the graph reads the static batch_dev
+            loss = graphed()
+            route()
+            return loss
 
     def barrier():
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
 
-    for _ in range(args.warmup):
-        step(batch_dev)
+    for _ in range(args.warmup):  # eager (lazy library initialisation happens here)
+        train(*batch_dev)
+        route()
+    if graphed is not None:  # first capture outside the timed region
+        graphed.capture()
     barrier()
 
     timer = ops.KernelTimer()
-    ops.set_kernel_timer(timer)
+    if graphed is None:
+        ops.set_kernel_timer(timer)
     clocks = Clocks(local_rank)
     clocks.start()
     l0 = N.launches["count"]
@@ -346,13 +372,27 @@ def run_ours(args, rank, world, local_rank):
     clk = clocks.stop()
     ops.set_kernel_timer(None)
     t_ms = e0.elapsed_time(e1)
+    timed_steps = args.steps
+    if graphed is not None:
+        # per-kernel CUDA-event timings need eager launches: a separate pass
+        timed_steps = min(args.steps, 5)
+        ops.set_kernel_timer(timer)
+        for _ in range(timed_steps):
+            train(*batch_dev)
+        torch.cuda.synchronize()
+        ops.set_kernel_timer(None)
     ksum = timer.summary()
 
     # end to end: host tokens (pinned) -> device every step, loss read back
     barrier()
     w0 = time.perf_counter()
     for _ in range(args.steps):
-        b = tuple(t.to(dev, non_blocking=True) for t in batch_host)
+        if graphed is not None:
+            for d, h in zip(batch_dev, batch_host):
+                d.copy_(h, non_blocking=True)
+            b = batch_dev
+        else:
+            b = tuple(t.to(dev, non_blocking=True) for t in batch_host)
         float(step(b).item())
     barrier()
     e2e_ms = (time.perf_counter() - w0) * 1e3
@@ -392,7 +432,8 @@ def run_ours(args, rank, world, local_rank):
                                 "GB/s": round(v["bytes"] / (v["ms"] * 1e-3) / 1e9, 1),
                                 "TFLOP/s": round(v["flops"] / (v["ms"] * 1e-3) / 1e12, 2)}
                             for k, v in ksum.items()},
-                "step_share": round(sum(v["ms"] for v in ksum.values()) / t_ms, 3)}
+                "step_share": round(sum(v["ms"] for v in ksum.values()) / timed_steps
+                                    / (t_ms / args.steps), 3)}
     line = {
         "metric": METRIC, "value": round(tokens / (t_ms * 1e-3), 1), "unit": wl.unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -404,6 +445,10 @@ def run_ours(args, rank, world, local_rank):
                 "h2d_bytes_per_step": wl.h2d_bytes(),
                 "d2h_bytes_per_step": 4},
         "gpu_launches": launches,
+        "cuda_graph": ({"captures": graphed.captures,
+                        "library_launches_per_replay": graphed.launches_per_replay,
+                        "kernel_timing": "eager pass of %d steps" % timed_steps}
+                       if graphed is not None else None),
         "clocks": clk,
         "router": {"algorithm": type(algo).__name__, "every_steps": algo.update_freq,
                    "update_plus_broadcast_ms": round(router_ms, 1),

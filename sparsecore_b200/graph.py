@@ -1,0 +1,70 @@
+"""CUDA-graph replay of a whole training step.
+
+A sparse training step launches a few hundred small kernels (SpMM, SDDMM,
+transposes, the cached-transpose refresh, the optimizer); for small models
+the host cost of those launches exceeds the GPU work.  ``GraphedStep``
+captures one step -- forward, backward, gradient exchange and optimizer, as
+written in the caller's ``step_fn`` -- into a CUDA graph over static input
+buffers and replays it.
+
+Topology changes (a SET / RigL update, a checkpoint load) rebuild each
+layer's cached transpose, whose buffers the graph would otherwise keep
+using, so the step is re-captured whenever any SparseLinear's
+``topology_version`` differs from the captured one; the transposes are
+rebuilt eagerly first (capture records, it does not execute).
+
+Requirements on ``step_fn``: it starts with ``optimizer.zero_grad(
+set_to_none=True)``, reads its inputs only from the static tensors given
+here, returns the loss tensor, and contains no host synchronisation (no
+``.item()``); the optimizer must be capturable (``AdamW(...,
+capturable=True)``; plain SGD is).  The step must have run eagerly at least
+once before the first capture (lazy library initialisation).  Router steps
+stay outside the graph.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native as N
+from . import ops
+from .nn import SparseLinear
+
+__all__ = ["GraphedStep"]
+
+
+class GraphedStep:
+    def __init__(self, model: torch.nn.Module, step_fn, static_inputs: tuple):
+        self.model = model
+        self.step_fn = step_fn
+        self.inputs = tuple(static_inputs)
+        self.layers = [m for m in model.modules() if isinstance(m, SparseLinear)]
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.loss: torch.Tensor | None = None
+        self._key = None
+        self.captures = 0
+        self.launches_per_replay = 0  # this library's kernels inside the graph
+
+    def _topology(self):
+        return tuple((id(m._csr), m._csr.topology_version) for m in self.layers)
+
+    def capture(self) -> None:
+        for m in self.layers:
+            ops._cached_transpose(m._csr)  # rebuild (eagerly) before recording
+        torch.cuda.synchronize()
+        self.graph = None  # release the previous graph's memory first
+        g = torch.cuda.CUDAGraph()
+        l0 = N.launches["count"]
+        with torch.cuda.graph(g):
+            self.loss = self.step_fn(*self.inputs)
+        self.launches_per_replay = N.launches["count"] - l0
+        N.launches["count"] = l0
+        self.graph = g
+        self._key = self._topology()
+        self.captures += 1
+
+    def __call__(self) -> torch.Tensor:
+        if self.graph is None or self._topology() != self._key:
+            self.capture()
+        self.graph.replay()
+        N.launches["count"] += self.launches_per_replay
+        return self.loss
