@@ -60,7 +60,9 @@ __device__ __forceinline__ void fma_vec(float v, float x, float* acc) { acc[0] =
 // slots per warp-wide load), so the next chunk's loads can be in flight while
 // the current chunk is computed.  rs/nn are held by the lanes of each row
 // group (lane r*LPR has row r's).  Slots past a row's nnz are not loaded.
-template <int LPR, int CH>
+// Rows are STRIDE pairs apart (CH + 1 by default; CH + 2 keeps every row
+// 16-byte aligned for paired 128-bit reads).
+template <int LPR, int CH, int STRIDE = CH + 1>
 struct SlotStager {
     static constexpr int RPW = 32 / LPR;
     static constexpr int ITER = RPW * CH / 32;
@@ -90,7 +92,7 @@ struct SlotStager {
 #pragma unroll
         for (int it = 0; it < ITER; ++it) {
             const int idx = it * 32 + lane;
-            st[(idx / CH) * (CH + 1) + idx % CH] = make_int2(c[it], __float_as_int(v[it]));
+            st[(idx / CH) * STRIDE + idx % CH] = make_int2(c[it], __float_as_int(v[it]));
         }
     }
 };
@@ -427,8 +429,10 @@ spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane / LPR, li = lane % LPR;
-    int2* st = stage + warp * RPW * (kXsCh + 1);
-    const int2* my = st + g * (kXsCh + 1);
+    constexpr int XST = kXsCh + 2;  // 16-byte aligned rows: two pairs per 128-bit read
+    int2* st = stage + warp * RPW * XST;
+    const int2* my = st + g * XST;
+    const int4* my4 = reinterpret_cast<const int4*>(my);
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
         fence_barrier_init();
@@ -476,15 +480,23 @@ spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
             for (int o = 16; o >= LPR; o >>= 1)
                 maxnn = max(maxnn, __shfl_xor_sync(0xffffffffu, maxnn, o));
             float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            SlotStager<LPR, kXsCh> sg;
+            SlotStager<LPR, kXsCh, XST> sg;
             if (maxnn > 0) sg.load(rs, nn, 0, cols, vals);
             for (int base = 0; base < maxnn; base += kXsCh) {
                 sg.store(st);
                 __syncwarp();
                 if (base + kXsCh < maxnn) sg.load(rs, nn, base + kXsCh, cols, vals);
                 const int cnt = min(kXsCh, nn - base);
-#pragma unroll 8
-                for (int t = 0; t < cnt; ++t) {
+                int t = 0;
+#pragma unroll 4
+                for (; t + 1 < cnt; t += 2) {
+                    const int4 e = my4[t >> 1];
+                    const float4 x0 = *reinterpret_cast<const float4*>(xcol + e.x * TN);
+                    const float4 x1 = *reinterpret_cast<const float4*>(xcol + e.z * TN);
+                    fma_vec(__int_as_float(e.y), x0, acc);
+                    fma_vec(__int_as_float(e.w), x1, acc);
+                }
+                if (t < cnt) {
                     const int2 e = my[t];
                     const float4 x = *reinterpret_cast<const float4*>(xcol + e.x * TN);
                     fma_vec(__int_as_float(e.y), x, acc);
@@ -519,7 +531,7 @@ int launch_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, c
     const int M = static_cast<int>(W->nrows);
     const int nbox = static_cast<int>((K + kXsBoxRows - 1) / kXsBoxRows);
     const size_t smem = static_cast<size_t>(nbox) * kXsBoxRows * TN * 4 +
-                        static_cast<size_t>(kXsWarps) * RPW * (kXsCh + 1) * sizeof(int2);
+                        static_cast<size_t>(kXsWarps) * RPW * (kXsCh + 2) * sizeof(int2);
     if (cudaFuncSetAttribute(spmm_xs_kernel<LPR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
         return -1;
