@@ -72,6 +72,12 @@ __device__ __forceinline__ int warp_sum(int v) {
 
 }  // namespace slb
 
+// Argument check: return SL_ERR_INVALID with "<fn>: <msg>" when cond fails.
+#define SL_REQUIRE(cond, fn, msg)                                            \
+    do {                                                                    \
+        if (!(cond)) return ::slb::fail(SL_ERR_INVALID, std::string(fn) + ": " + (msg)); \
+    } while (0)
+
 #define SL_RETURN_IF_LAUNCH_FAILED(what)                                   \
     do {                                                                  \
         cudaError_t e_ = cudaGetLastError();                              \

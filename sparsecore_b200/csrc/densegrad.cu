@@ -103,6 +103,8 @@ extern "C" int sl_dense_grad(const float* dY, const float* X, int64_t M, int64_t
         return fail(SL_ERR_INVALID, "dense_grad: shape params must be non-negative");
     if (M > INT_MAX || K > INT_MAX) return fail(SL_ERR_UNSUPPORTED, "dense_grad: shape beyond int32");
     if (M == 0 || K == 0) return SL_OK;
+    SL_REQUIRE(G != nullptr, "dense_grad", "NULL output G");
+    SL_REQUIRE(N == 0 || (dY != nullptr && X != nullptr), "dense_grad", "NULL dense operand");
     cudaStream_t s = as_stream(stream);
     if (N == 0) return cuda_status(cudaMemsetAsync(G, 0, sizeof(float) * M * K, s), "dense_grad memset");
     const dim3 grid(static_cast<unsigned>((K + BK - 1) / BK), static_cast<unsigned>((M + BM - 1) / BM));

@@ -322,6 +322,11 @@ int launch_rewrite(const sl_csr* W, const float* thr_dev, const int32_t* force_i
                                             " exceeds the supported maximum of " +
                                             std::to_string(kMaxDstCols));
     if (W->nrows == 0) return SL_OK;
+    SL_REQUIRE(thr_dev != nullptr && force_idx != nullptr, fn, "NULL threshold or force_idx");
+    SL_REQUIRE(MODE == kGrowTopK || (grow_off != nullptr && grow_list != nullptr), fn,
+               "NULL grow_offsets or grow list");
+    SL_REQUIRE(MODE != kGrowTopK || (G != nullptr && row_flag != nullptr), fn, "NULL G or row_flag");
+    SL_REQUIRE(MODE != kGrowCols || row_mask != nullptr, fn, "NULL row_mask");
     const int K = static_cast<int>(W->ncols);
     const size_t smem = 9 * static_cast<size_t>(K > 0 ? K : 1);
     if (smem > 48 * 1024)
@@ -351,6 +356,7 @@ int64_t sl_dst_max_ncols(void) { return kMaxDstCols; }
 int sl_dst_threshold(const sl_csr* W, int64_t k, float* thr_dev, void* scratch, void* stream) {
     if (int rc = check_csr(W, "sl_dst_threshold")) return rc;
     if (k < 1) return fail(SL_ERR_INVALID, "sl_dst_threshold: k must be >= 1");
+    SL_REQUIRE(thr_dev != nullptr && scratch != nullptr, "sl_dst_threshold", "NULL output or scratch");
     cudaStream_t s = as_stream(stream);
     unsigned* hist = static_cast<unsigned*>(scratch);
     SelectState* st = reinterpret_cast<SelectState*>(hist + 256);
@@ -373,6 +379,8 @@ int sl_dst_keep(const sl_csr* W, const float* thr_dev, int32_t* n_keep, int32_t*
                 void* stream) {
     if (int rc = check_csr(W, "sl_dst_keep")) return rc;
     if (W->nrows == 0) return SL_OK;
+    SL_REQUIRE(thr_dev != nullptr && n_keep != nullptr && force_idx != nullptr, "sl_dst_keep",
+               "NULL threshold or output array");
     keep_kernel<<<row_grid(W->nrows), kDstThreads, 0, as_stream(stream)>>>(
         static_cast<int>(W->nrows), W->row_start, W->row_nnz, W->values, thr_dev, n_keep,
         force_idx);

@@ -147,6 +147,10 @@ int sl_dense_count(const float* dense, int64_t M, int64_t K, float threshold,
     if (M < 0 || K < 0) return fail(SL_ERR_INVALID, "sl_dense_count: negative shape");
     if (M > INT_MAX || K > INT_MAX)
         return fail(SL_ERR_UNSUPPORTED, "sl_dense_count: shape beyond int32");
+    SL_REQUIRE(M == 0 || K == 0 || dense != nullptr, "sl_dense_count", "NULL dense input");
+    SL_REQUIRE(M == 0 || (row_nnz != nullptr && row_capacity != nullptr && row_start != nullptr),
+               "sl_dense_count", "NULL row array");
+    SL_REQUIRE(out_total_dev != nullptr, "sl_dense_count", "NULL out_total_dev");
     cudaStream_t s = as_stream(stream);
     if (M > 0) {
         dense_count_kernel<<<row_grid(M), 256, 0, s>>>(dense, static_cast<int>(M), K, threshold,
@@ -160,6 +164,7 @@ int sl_dense_count(const float* dense, int64_t M, int64_t K, float threshold,
 int sl_dense_fill(const float* dense, float threshold, const sl_csr* out, void* stream) {
     if (int rc = check_csr(out, "sl_dense_fill")) return rc;
     if (out->nrows == 0) return SL_OK;
+    SL_REQUIRE(out->ncols == 0 || dense != nullptr, "sl_dense_fill", "NULL dense input");
     dense_fill_kernel<<<row_grid(out->nrows), 256, 0, as_stream(stream)>>>(
         dense, static_cast<int>(out->nrows), out->ncols, threshold, out->row_start,
         out->row_capacity, out->values, out->col_indices);
@@ -172,6 +177,7 @@ int sl_to_dense(const sl_csr* W, float* dense, void* stream) {
     cudaStream_t s = as_stream(stream);
     const size_t bytes = sizeof(float) * static_cast<size_t>(W->nrows) * W->ncols;
     if (bytes == 0) return SL_OK;
+    SL_REQUIRE(dense != nullptr, "sl_to_dense", "NULL output");
     if (int rc = cuda_status(cudaMemsetAsync(dense, 0, bytes, s), "sl_to_dense memset")) return rc;
     to_dense_kernel<<<row_grid(W->nrows), 256, 0, s>>>(static_cast<int>(W->nrows), W->ncols,
                                                        W->row_start, W->row_nnz, W->col_indices,
@@ -182,6 +188,7 @@ int sl_to_dense(const sl_csr* W, float* dense, void* stream) {
 
 int sl_check_invariants(const sl_csr* W, int64_t n_slots, int64_t* report, void* stream) {
     if (int rc = check_csr(W, "sl_check_invariants")) return rc;
+    SL_REQUIRE(report != nullptr, "sl_check_invariants", "NULL report");
     cudaStream_t s = as_stream(stream);
     if (int rc = cuda_status(cudaMemsetAsync(report, 0x7f, 4 * sizeof(int64_t), s),
                              "sl_check_invariants memset"))

@@ -197,6 +197,7 @@ int sl_device_status(int reset, unsigned* out) {
 int sl_exclusive_scan(const int32_t* counts, int64_t n, int32_t* out, int64_t* total_dev,
                       void* stream) {
     if (n < 0) return fail(SL_ERR_INVALID, "sl_exclusive_scan: negative n");
+    SL_REQUIRE(n == 0 || (counts != nullptr && out != nullptr), "sl_exclusive_scan", "NULL array");
     exclusive_scan_kernel<<<1, kScanThreads, 0, as_stream(stream)>>>(counts, n, out, total_dev);
     SL_RETURN_IF_LAUNCH_FAILED("sl_exclusive_scan");
     return SL_OK;
@@ -208,6 +209,9 @@ int sl_capacity_scan(const int32_t* row_nnz, int64_t n, double one_plus_padding_
     if (n < 0) return fail(SL_ERR_INVALID, "sl_capacity_scan: negative n");
     if (!(one_plus_padding_ratio >= 1.0))
         return fail(SL_ERR_INVALID, "sl_capacity_scan: padding_ratio must be >= 0");
+    SL_REQUIRE(n == 0 || (row_nnz != nullptr && row_capacity != nullptr && row_start != nullptr),
+               "sl_capacity_scan", "NULL row array");
+    SL_REQUIRE(out_total_dev != nullptr, "sl_capacity_scan", "NULL out_total_dev");
     capacity_scan_kernel<<<1, kScanThreads, 0, as_stream(stream)>>>(
         row_nnz, n, one_plus_padding_ratio, row_capacity, row_start, out_total_dev);
     SL_RETURN_IF_LAUNCH_FAILED("sl_capacity_scan");
@@ -218,6 +222,8 @@ int sl_pack_live(const sl_csr* W, const int32_t* packed_offsets, const float* sr
                  void* stream) {
     if (int rc = check_csr(W, "sl_pack_live")) return rc;
     if (W->nrows == 0) return SL_OK;
+    SL_REQUIRE(packed_offsets != nullptr && src != nullptr && dst != nullptr, "sl_pack_live",
+               "NULL array");
     pack_live_kernel<<<row_grid(W->nrows), 256, 0, as_stream(stream)>>>(
         static_cast<int>(W->nrows), W->row_start, W->row_nnz, packed_offsets, src, dst);
     SL_RETURN_IF_LAUNCH_FAILED("sl_pack_live");
@@ -228,6 +234,8 @@ int sl_unpack_live(const sl_csr* W, const int32_t* packed_offsets, const float* 
                    float scale, void* stream) {
     if (int rc = check_csr(W, "sl_unpack_live")) return rc;
     if (W->nrows == 0) return SL_OK;
+    SL_REQUIRE(packed_offsets != nullptr && src != nullptr && dst != nullptr, "sl_unpack_live",
+               "NULL array");
     unpack_live_kernel<<<row_grid(W->nrows), 256, 0, as_stream(stream)>>>(
         static_cast<int>(W->nrows), W->row_start, W->row_nnz, packed_offsets, src, dst, scale);
     SL_RETURN_IF_LAUNCH_FAILED("sl_unpack_live");

@@ -143,6 +143,12 @@ int sl_transpose_count(const sl_csr* W, double one_plus_padding_ratio, int32_t* 
                                             std::to_string(kMaxSharedCols));
     if (!(one_plus_padding_ratio >= 1.0))
         return fail(SL_ERR_INVALID, "sl_transpose_count: padding_ratio must be >= 0");
+    SL_REQUIRE(W->ncols == 0 || (out_row_nnz != nullptr && out_row_capacity != nullptr &&
+                                 out_row_start != nullptr),
+               "sl_transpose_count", "NULL output row array");
+    SL_REQUIRE(out_total_dev != nullptr, "sl_transpose_count", "NULL out_total_dev");
+    SL_REQUIRE(W->nrows == 0 || W->ncols == 0 || scratch != nullptr, "sl_transpose_count",
+               "NULL scratch");
     cudaStream_t s = as_stream(stream);
     const int M = static_cast<int>(W->nrows), K = static_cast<int>(W->ncols);
     if (K == 0) {
@@ -182,6 +188,9 @@ int sl_transpose_fill(const sl_csr* W, const sl_csr* WT, int64_t* perm, const vo
         return fail(SL_ERR_INVALID, "sl_transpose_fill: WT shape must be W's swapped");
     if (W->ncols > kMaxSharedCols)
         return fail(SL_ERR_UNSUPPORTED, "sl_transpose_fill: ncols too large");
+    SL_REQUIRE(WT->total_capacity == 0 || perm != nullptr, "sl_transpose_fill", "NULL perm");
+    SL_REQUIRE(W->nrows == 0 || W->ncols == 0 || scratch != nullptr, "sl_transpose_fill",
+               "NULL scratch");
     cudaStream_t s = as_stream(stream);
     const int M = static_cast<int>(W->nrows), K = static_cast<int>(W->ncols);
     const int64_t capT = WT->total_capacity;
@@ -205,6 +214,7 @@ int sl_transpose_fill(const sl_csr* W, const sl_csr* WT, int64_t* perm, const vo
 int sl_values_gather(const int64_t* perm, const float* src, float* dst, int64_t n, void* stream) {
     if (n < 0) return fail(SL_ERR_INVALID, "sl_values_gather: negative n");
     if (n == 0) return SL_OK;
+    SL_REQUIRE(perm != nullptr && src != nullptr && dst != nullptr, "sl_values_gather", "NULL array");
     gather_kernel<<<grid_for(n), kTrThreads, 0, as_stream(stream)>>>(perm, src, dst, n);
     SL_RETURN_IF_LAUNCH_FAILED("sl_values_gather");
     return SL_OK;
