@@ -207,6 +207,7 @@ class _SparseLinearFunction(torch.autograd.Function):
         X = _transpose(x)
         ctx.save_for_backward(W_values, X)
         ctx.W = W
+        ctx.param = W_values
         return _transpose(_spmm_raw(W, X))
 
     @staticmethod
@@ -214,11 +215,70 @@ class _SparseLinearFunction(torch.autograd.Function):
         W_values, X = ctx.saved_tensors
         W = ctx.W
         dY = _transpose(dy)
-        dW = _sddmm_raw(W, dY, X) if ctx.needs_input_grad[0] else None
+        dW = None
+        if ctx.needs_input_grad[0]:
+            param = ctx.param
+            if _async_weight_grad and param.is_leaf:
+                _sddmm_on_side_stream(W, dY, X, param)
+            else:
+                dW = _sddmm_raw(W, dY, X)
         dx = None
         if ctx.needs_input_grad[2]:
             dx = _transpose(_spmm_raw(_cached_transpose(W), dY, kind="spmm_dx"))
         return dW, None, dx
+
+
+# ── weight gradient off the critical path ───────────────────────────────
+# The SDDMM's output is consumed only by the optimizer step, while dX gates
+# the rest of the backward pass.  SparseLinear therefore launches the SDDMM
+# on a per-device side stream (forked from the current stream after dY is
+# ready), so it overlaps the following dX / attention / transpose work, and
+# joins it back at the end of the backward pass (an autograd engine
+# callback, as DistributedDataParallel does): the current stream waits for
+# the SDDMM and the gradient is accumulated into the Parameter's ``.grad``
+# there.  Values are identical to the synchronous path.
+_async_weight_grad = True
+_side_streams: dict = {}
+
+
+def set_async_weight_grad(enabled: bool) -> None:
+    """Run SparseLinear's weight-gradient SDDMM on a side stream (default)."""
+    global _async_weight_grad
+    _async_weight_grad = bool(enabled)
+
+
+def _side_stream(device: torch.device) -> torch.cuda.Stream:
+    s = _side_streams.get(device.index)
+    if s is None:
+        s = torch.cuda.Stream(device=device)
+        _side_streams[device.index] = s
+    return s
+
+
+def _sddmm_on_side_stream(W: PaddedCSR, dY: torch.Tensor, X: torch.Tensor, param) -> None:
+    main = torch.cuda.current_stream(dY.device)
+    side = _side_stream(dY.device)
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        dW = _sddmm_raw(W, dY, X)
+        done = torch.cuda.Event()
+        done.record(side)
+    capturing = torch.cuda.is_current_stream_capturing()
+    keep = (dY, X)  # alive until the join: no allocation may reuse them while the SDDMM reads
+
+    def join():
+        cur = torch.cuda.current_stream(dW.device)
+        cur.wait_event(done)  # frees of `keep` after this point are ordered after the SDDMM
+        if not capturing:
+            dW.record_stream(cur)  # dW's block belongs to the side stream's pool
+        if param.grad is None:
+            param.grad = dW
+        else:
+            param.grad.add_(dW)
+        del keep[:]
+
+    keep = list(keep)
+    torch.autograd.Variable._execution_engine.queue_callback(join)
 
 
 def spmm(W: PaddedCSR, X: torch.Tensor, *, kernel: str = "auto") -> torch.Tensor:
