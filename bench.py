@@ -45,6 +45,10 @@ def parse():
     ap.add_argument("--graph", action="store_true",
                     help="replay the training step as a CUDA graph (re-captured after "
                          "topology updates); per-kernel timings then come from an eager pass")
+    ap.add_argument("--stream", choices=["priority", "default"], default="priority",
+                    help="stream for the training step: a high-priority stream (default; the "
+                         "weight-gradient SDDMM side stream keeps the lowest priority, so "
+                         "critical-path kernels get SMs first) or torch's default stream")
     ap.add_argument("--sweep", action="store_true",
                     help="config-3 standalone SpMM sweep: one JSON line per cell")
     return ap.parse_args()
@@ -308,6 +312,10 @@ def run_ours(args, rank, world, local_rank):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
+    if args.stream == "priority":
+        from sparsecore_b200.ops import critical_path_stream
+
+        torch.cuda.set_stream(critical_path_stream(dev))
     wl = Workload(args.workload, dev, rank, capturable=args.graph)
     model, algo, opt = wl.model, wl.algo, wl.opt
     ddp = SparseDataParallel(model)

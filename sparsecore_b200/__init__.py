@@ -16,7 +16,7 @@ import torch as _torch  # noqa: F401
 
 from . import layout
 from .layout import PaddedCSR, transpose_with_perm
-from .ops import spmm
+from .ops import critical_path_stream, set_async_weight_grad, spmm
 from .nn import SparseLinear
 from .router import SparsityAlgorithm, Static, DynamicSparsityAlgorithm, SET, RigL, dense_grad
 
@@ -31,5 +31,7 @@ __all__ = [
     "RigL",
     "dense_grad",
     "transpose_with_perm",
+    "critical_path_stream",
+    "set_async_weight_grad",
 ]
 __version__ = "0.1.0"

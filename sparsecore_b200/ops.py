@@ -247,6 +247,21 @@ def set_async_weight_grad(enabled: bool) -> None:
     _async_weight_grad = bool(enabled)
 
 
+def critical_path_stream(device=None) -> torch.cuda.Stream:
+    """A highest-priority CUDA stream for running a training step.
+
+    SparseLinear's weight-gradient SDDMM runs on a side stream of the lowest
+    (default) priority; when the step itself runs on this stream, the block
+    scheduler hands freed SM slots to the critical-path kernels (dX, the
+    rest of the backward pass) first.  Measured on B200, config 5: 123.7 ->
+    118.5 ms/step.  Use as ``torch.cuda.set_stream(critical_path_stream())``
+    or ``with torch.cuda.stream(critical_path_stream()):``.
+    """
+    dev = N.require_cuda(device)
+    _, hi = torch.cuda.Stream.priority_range()
+    return torch.cuda.Stream(device=dev, priority=hi)
+
+
 def _side_stream(device: torch.device) -> torch.cuda.Stream:
     s = _side_streams.get(device.index)
     if s is None:
