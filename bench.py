@@ -318,6 +318,7 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.set_stream(critical_path_stream(dev))
     wl = Workload(args.workload, dev, rank, capturable=args.graph)
     model, algo, opt = wl.model, wl.algo, wl.opt
+    ops.set_async_weight_grad(True)  # the loop below reads .grad after backward()
     ddp = SparseDataParallel(model)
     batch_host = tuple(t.pin_memory() for t in wl.batch)
     batch_dev = tuple(t.to(dev) for t in batch_host)

@@ -236,13 +236,20 @@ class _SparseLinearFunction(torch.autograd.Function):
 # joins it back at the end of the backward pass (an autograd engine
 # callback, as DistributedDataParallel does): the current stream waits for
 # the SDDMM and the gradient is accumulated into the Parameter's ``.grad``
-# there.  Values are identical to the synchronous path.
-_async_weight_grad = True
+# there.  Values are identical to the synchronous path.  Opt-in: with it the
+# weight gradient reaches the Parameter only through ``.grad`` at the end of
+# ``backward()`` -- ``torch.autograd.grad`` on the weights and hooks
+# registered on the weight Parameter do not see it -- so the default keeps
+# plain autograd semantics.
+_async_weight_grad = False
 _side_streams: dict = {}
 
 
 def set_async_weight_grad(enabled: bool) -> None:
-    """Run SparseLinear's weight-gradient SDDMM on a side stream (default)."""
+    """Run SparseLinear's weight-gradient SDDMM on a side stream, overlapped
+    with the rest of the backward pass; the gradient is accumulated into the
+    weight Parameter's ``.grad`` when ``backward()`` finishes (not visible to
+    ``torch.autograd.grad`` or Parameter hooks).  Off by default."""
     global _async_weight_grad
     _async_weight_grad = bool(enabled)
 

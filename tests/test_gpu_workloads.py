@@ -13,12 +13,15 @@ from gpu_helpers import dev
 pytestmark = pytest.mark.gpu
 
 
-def _run(cfg, steps, graph):
+def _run(cfg, steps, graph, async_dw=False):
     import sparsecore_b200 as sl
     from sparsecore_b200.dist import SparseDataParallel, sync_after_router_step
     from sparsecore_b200.graph import GraphedStep
     from sparsecore_b200.workloads import MiniGPT, lm_loss, synthetic_tokens
 
+    from sparsecore_b200 import ops
+
+    ops.set_async_weight_grad(async_dw)
     torch.manual_seed(0)
     model = MiniGPT(cfg, device=dev())
     algo_cls = sl.SET if cfg.router == "SET" else sl.RigL
@@ -48,6 +51,7 @@ def _run(cfg, steps, graph):
         losses.append(float(loss.item()))
         algo.step()
         sync_after_router_step(ddp, algo)
+    ops.set_async_weight_grad(False)
     return losses, layers, versions0
 
 
@@ -63,5 +67,30 @@ def test_transformer_workload_trains_across_router_update(name):
         m._csr.assert_invariants()
         assert m._values.data_ptr() == m._csr.values.data_ptr()
         assert m._csr.topology_version > v  # the update at step 3 rewrote the rows
-    graphed, _, _ = _run(cfg, 5, graph=True)
-    assert graphed == losses
+    # Side-stream weight gradient: same values, eager and graph-replayed.
+    # At ctx 512 (config 5) torch's fp32 memory-efficient attention backward
+    # accumulates with atomics, so two identical runs already differ in the
+    # last bits (measured: ~1e-11 in the dense gradients); config 4 (ctx 256)
+    # is deterministic and must match exactly.
+    overlapped, _, _ = _run(cfg, 5, graph=False, async_dw=True)
+    graphed, _, _ = _run(cfg, 5, graph=True, async_dw=True)
+    for other in (overlapped, graphed):
+        if name == "cfg4":
+            assert other == losses
+        else:
+            assert other == pytest.approx(losses, rel=1e-5, abs=1e-6)
+
+
+def test_autograd_grad_sees_the_weight_gradient_by_default():
+    """Default (synchronous) path: torch.autograd.grad and Parameter hooks see
+    dW, as with the reference's _SpMMFunction."""
+    import sparsecore_b200 as sl
+
+    torch.manual_seed(0)
+    layer = sl.SparseLinear(32, 16, sparsity=0.8)
+    x = torch.randn(8, 32, device=dev())
+    seen = []
+    layer._values.register_hook(lambda g: seen.append(g.clone()))
+    (gw,) = torch.autograd.grad(layer(x).square().sum(), [layer._values])
+    assert gw.shape == layer._values.shape and torch.count_nonzero(gw) > 0
+    assert len(seen) == 1 and torch.equal(seen[0], gw)
