@@ -3,7 +3,7 @@
 Run here (where the reference sources are mounted), never on the GPU box:
 
     make -C oracle ref                       # builds oracle/_ref/refcore/_core*.so
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref <reference source tree>]
 
 The reference's Python package is imported from its own source tree, with
 its compiled `_core` taken from oracle/_ref/refcore (built from the
