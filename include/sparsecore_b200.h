@@ -60,6 +60,12 @@ SL_API const char* sl_version(void);
  * device-side wait (TMA / mbarrier) gave up instead of hanging; that call's
  * output is invalid.  reset != 0 clears the word after reading. */
 SL_API int sl_device_status(int reset, unsigned* out);
+/* Self-test of the bounded device waits (no reference counterpart): launches
+ * one warp that waits on an mbarrier nothing completes; after `spins` polls
+ * (1 .. 2^24) the wait gives up, raises bit 0 of the status word and the
+ * kernel returns -- the context stays usable.  Read it with
+ * sl_device_status. */
+SL_API int sl_selftest_bounded_wait(int64_t spins, void* stream);
 
 /* ── Forward SpMM ─────────────────────────────────────────────────────────
  * Y[M,N] = W[M,K] . X[K,N].  Each Y element is the fp32 FMA chain over the

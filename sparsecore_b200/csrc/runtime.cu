@@ -165,6 +165,18 @@ unsigned* device_status_word() {
     return words[dev];
 }
 
+// Self-test of the bounded waits: one thread waits on an mbarrier that no
+// arrival will ever complete; after `spins` polls the wait gives up, raises
+// the status word and the kernel returns.
+__global__ void bounded_wait_selftest_kernel(unsigned* status, long long spins) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+        mbar_wait(&bar, 0u, status, spins);  // phase 0 never completes: times out
+    }
+}
+
 int row_grid(int64_t M) {
     const int64_t want = (M + 7) / 8;
     const int64_t cap = static_cast<int64_t>(num_sms()) * 16;
@@ -191,6 +203,16 @@ int sl_device_status(int reset, unsigned* out) {
     if (reset && v)
         if (int rc = cuda_status(cudaMemset(w, 0, sizeof(unsigned)), "sl_device_status")) return rc;
     if (out) *out = v;
+    return SL_OK;
+}
+
+int sl_selftest_bounded_wait(int64_t spins, void* stream) {
+    if (spins < 1 || spins > (int64_t(1) << 24))
+        return fail(SL_ERR_INVALID, "sl_selftest_bounded_wait: spins must be in [1, 2^24]");
+    unsigned* w = device_status_word();
+    if (w == nullptr) return fail(SL_ERR_CUDA, "sl_selftest_bounded_wait: no device status word");
+    bounded_wait_selftest_kernel<<<1, 32, 0, as_stream(stream)>>>(w, spins);
+    SL_RETURN_IF_LAUNCH_FAILED("sl_selftest_bounded_wait");
     return SL_OK;
 }
 

@@ -55,9 +55,10 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 }
 
 // Returns false on timeout (and raises bit 0 of *status).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned phase, unsigned* status) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned phase, unsigned* status,
+                                          long long spin_limit = kSpinLimit) {
     const uint32_t a = smem_addr(bar);
-    for (long long it = 0; it < kSpinLimit; ++it) {
+    for (long long it = 0; it < spin_limit; ++it) {
         uint32_t done;
         asm volatile(
             "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
