@@ -17,13 +17,14 @@ import torch as _torch  # noqa: F401
 from . import layout
 from .layout import PaddedCSR, transpose_with_perm
 from .ops import critical_path_stream, set_async_weight_grad, spmm
-from .nn import SparseLinear
+from .nn import SparseLinear, sparse_mlp
 from .router import SparsityAlgorithm, Static, DynamicSparsityAlgorithm, SET, RigL, dense_grad
 
 __all__ = [
     "PaddedCSR",
     "spmm",
     "SparseLinear",
+    "sparse_mlp",
     "SparsityAlgorithm",
     "DynamicSparsityAlgorithm",
     "Static",

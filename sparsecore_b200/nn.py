@@ -18,9 +18,9 @@ import torch.nn as nn
 
 from . import _native as N
 from .layout import PaddedCSR, from_dense
-from .ops import _SparseLinearFunction
+from .ops import _SparseLinearFunction, _SparseMLPFunction
 
-__all__ = ["SparseLinear"]
+__all__ = ["SparseLinear", "sparse_mlp"]
 
 
 class SparseLinear(nn.Module):
@@ -109,3 +109,31 @@ class SparseLinear(nn.Module):
     def extra_repr(self) -> str:
         return (f"in_features={self.in_features}, out_features={self.out_features}, "
                 f"bias={self.bias is not None}, sparsity={self.sparsity}, nnz={self.nnz}")
+
+
+def _plain(layer: SparseLinear) -> bool:
+    return (layer.bias is None and not layer._forward_hooks and not layer._forward_pre_hooks
+            and not layer._backward_hooks and not getattr(layer, "_backward_pre_hooks", None))
+
+
+def sparse_mlp(x: torch.Tensor, fc1: SparseLinear, fc2: SparseLinear,
+               activation: str = "gelu") -> torch.Tensor:
+    """``fc2(act(fc1(x)))`` for two SparseLinears with ``activation`` in
+    {"gelu", "relu"}.  When both layers are bias-free and carry no module
+    hooks (RigL's gradient capture uses hooks), the hidden activation stays
+    in the kernels' column-per-token layout (``ops._SparseMLPFunction``);
+    otherwise the two layers are called as modules.  Same values either way.
+    """
+    if activation not in ("gelu", "relu"):
+        raise ValueError(f"sparse_mlp: activation must be 'gelu' or 'relu', got {activation!r}")
+    if fc1.out_features != fc2.in_features:
+        raise ValueError(f"sparse_mlp: fc1.out_features={fc1.out_features} != "
+                         f"fc2.in_features={fc2.in_features}")
+    if not (_plain(fc1) and _plain(fc2)) or x.shape[-1] != fc1.in_features:
+        h = fc1(x)
+        h = torch.nn.functional.gelu(h) if activation == "gelu" else torch.relu(h)
+        return fc2(h)
+    shp = x.shape
+    y = _SparseMLPFunction.apply(fc1._values, fc2._values, x.reshape(-1, fc1.in_features),
+                                 fc1._csr, fc2._csr, activation)
+    return y.reshape(shp[:-1] + (fc2.out_features,))

@@ -215,13 +215,7 @@ class _SparseLinearFunction(torch.autograd.Function):
         W_values, X = ctx.saved_tensors
         W = ctx.W
         dY = _transpose(dy)
-        dW = None
-        if ctx.needs_input_grad[0]:
-            param = ctx.param
-            if _async_weight_grad and param.is_leaf:
-                _sddmm_on_side_stream(W, dY, X, param)
-            else:
-                dW = _sddmm_raw(W, dY, X)
+        dW = _weight_grad(W, dY, X, ctx.param, ctx.needs_input_grad[0])
         dx = None
         if ctx.needs_input_grad[2]:
             dx = _transpose(_spmm_raw(_cached_transpose(W), dY, kind="spmm_dx"))
@@ -301,6 +295,54 @@ def _sddmm_on_side_stream(W: PaddedCSR, dY: torch.Tensor, X: torch.Tensor, param
 
     keep = list(keep)
     torch.autograd.Variable._execution_engine.queue_callback(join)
+
+
+def _weight_grad(W: PaddedCSR, dY: torch.Tensor, X: torch.Tensor, param, needed: bool):
+    """dW for a SparseLinear weight: async (side stream, joined at the end of
+    backward) when enabled, else returned for autograd to accumulate."""
+    if not needed:
+        return None
+    if _async_weight_grad and param.is_leaf:
+        _sddmm_on_side_stream(W, dY, X, param)
+        return None
+    return _sddmm_raw(W, dY, X)
+
+
+class _SparseMLPFunction(torch.autograd.Function):
+    """Two bias-free SparseLinears with an element-wise activation between
+    them, ``y = W2 . act(W1 . x^T)``, keeping the hidden activation in the
+    kernels' column-per-token layout: the transposes of the hidden tensor
+    that two separate SparseLinear calls would make (one each way, forward
+    and backward) are skipped.  Every value equals the unfused composition
+    (the activation and its backward are element-wise)."""
+
+    @staticmethod
+    def forward(ctx, v1, v2, x, W1, W2, act):
+        X = _transpose(x)
+        Y1 = _spmm_raw(W1, X)
+        H = torch.nn.functional.gelu(Y1) if act == "gelu" else torch.relu(Y1)
+        Y2 = _spmm_raw(W2, H)
+        ctx.save_for_backward(X, Y1, H)
+        ctx.W1, ctx.W2, ctx.act = W1, W2, act
+        ctx.p1, ctx.p2 = v1, v2
+        return _transpose(Y2)
+
+    @staticmethod
+    def backward(ctx, dy):
+        X, Y1, H = ctx.saved_tensors
+        W1, W2 = ctx.W1, ctx.W2
+        dY2 = _transpose(dy)
+        dW2 = _weight_grad(W2, dY2, H, ctx.p2, ctx.needs_input_grad[1])
+        dH = _spmm_raw(_cached_transpose(W2), dY2, kind="spmm_dx")
+        if ctx.act == "gelu":
+            dY1 = torch.ops.aten.gelu_backward(dH, Y1)
+        else:
+            dY1 = torch.ops.aten.threshold_backward(dH, H, 0)
+        dW1 = _weight_grad(W1, dY1, X, ctx.p1, ctx.needs_input_grad[0])
+        dx = None
+        if ctx.needs_input_grad[2]:
+            dx = _transpose(_spmm_raw(_cached_transpose(W1), dY1, kind="spmm_dx"))
+        return dW1, dW2, dx, None, None, None
 
 
 def spmm(W: PaddedCSR, X: torch.Tensor, *, kernel: str = "auto") -> torch.Tensor:

@@ -22,7 +22,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .nn import SparseLinear
+from .nn import SparseLinear, sparse_mlp
 
 
 @dataclass(frozen=True)
@@ -80,6 +80,8 @@ class SparseFFN(nn.Module):
         self.fc_down = linear(d_ff, d_model, sparsity)
 
     def forward(self, x):
+        if isinstance(self.fc_up, SparseLinear) and isinstance(self.fc_down, SparseLinear):
+            return sparse_mlp(x, self.fc_up, self.fc_down, "gelu")
         return self.fc_down(F.gelu(self.fc_up(x)))
 
 
