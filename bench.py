@@ -39,7 +39,8 @@ def parse():
     ap.add_argument("--cpu-seqs", type=int, default=2, help="sequences per CPU sample step")
     ap.add_argument("--kernel", default=None,
                     help="profiling mode: SHAPE:KIND:N runs 2 launches of one kernel "
-                         "(SHAPE in %s or MxK@sparsity; KIND fwd|dw|dx|transpose)" % list(SHAPES))
+                         "(SHAPE in %s or MxK@sparsity; KIND fwd|dw|dx|transpose|densegrad, or "
+                         "set|rigl for two router updates)" % list(SHAPES))
     ap.add_argument("--workload", choices=["cfg5", "cfg4", "cfg2"], default="cfg5",
                     help="training workload (default cfg5, the headline configuration)")
     ap.add_argument("--graph", action="store_true",
@@ -88,13 +89,24 @@ def run_kernel_case(spec):
     X = torch.randn(K, N, device="cuda")
     dY = torch.randn(M, N, device="cuda")
     WT, _ = sl.transpose_with_perm(W)
-    for _ in range(2):
+    if kind in ("set", "rigl"):
+        # one router update on a SparseLinear of this shape (its CSR = W)
+        layer = sl.SparseLinear(K, M, bias=False, sparsity=s)
+        algo = (sl.SET if kind == "set" else sl.RigL)(sparsity=s, update_freq=1, seed=0)
+        layer.apply(algo)
+        xin = torch.randn(N, K, device="cuda")
+        for _ in range(2):
+            layer(xin).square().sum().backward()
+            algo.update()
+    for _ in range(2 if kind not in ("set", "rigl") else 0):
         if kind == "fwd":
             ops._spmm_raw(W, X)
         elif kind == "dw":
             ops._sddmm_raw(W, dY, X)
         elif kind == "dx":
             ops._spmm_raw(WT, dY)
+        elif kind == "densegrad":
+            sl.dense_grad(dY, X)
         else:
             sl.transpose_with_perm(W)
     torch.cuda.synchronize()
