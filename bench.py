@@ -227,9 +227,16 @@ class Workload:
             cfg = W.CFG5 if name == "cfg5" else W.CFG4
             self.cfg = cfg
             self.model = W.MiniGPT(cfg, device=dev, linear=linear)
-            algo_cls = sl.SET if cfg.router == "SET" else sl.RigL
-            self.algo = algo_cls(sparsity=cfg.ffn_sparsity, drop_fraction=cfg.drop_fraction,
-                                 update_freq=cfg.update_freq, seed=0)
+            if cfg.router == "SET":
+                self.algo = sl.SET(sparsity=cfg.ffn_sparsity, drop_fraction=cfg.drop_fraction,
+                                   update_freq=cfg.update_freq, seed=0)
+            else:
+                # Eager steps clone X / dY only on update steps (same topology
+                # as cloning every step); a replayed graph runs no hooks, so the
+                # clones must be recorded into it on every step.
+                self.algo = sl.RigL(sparsity=cfg.ffn_sparsity, drop_fraction=cfg.drop_fraction,
+                                    update_freq=cfg.update_freq, seed=0,
+                                    capture="every_step" if capturable else "update_step")
             self.opt = torch.optim.AdamW(self.model.parameters(), lr=cfg.lr,
                                          capturable=capturable)
             nb = batch or cfg.batch

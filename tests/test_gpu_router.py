@@ -65,6 +65,36 @@ def test_rigl_end_to_end_captures_and_grows():
     layer._csr.assert_invariants()
 
 
+def test_rigl_update_step_capture_matches_every_step():
+    """capture="update_step" clones X / dY only before an update, and the
+    rewritten topology is the same as with the reference's every-step
+    capture."""
+    import sparsecore_b200 as sl
+
+    out = {}
+    for mode in ("every_step", "update_step"):
+        torch.manual_seed(0)
+        layer = sl.SparseLinear(96, 48, sparsity=0.85)
+        opt = torch.optim.SGD(layer.parameters(), lr=0.1)
+        algo = sl.RigL(sparsity=0.85, drop_fraction=0.3, update_freq=3, seed=4, capture=mode)
+        layer.apply(algo)
+        xs = torch.randn(7, 20, 96, device=dev()).unbind(0)
+        n_cap = []
+        for x in xs:
+            opt.zero_grad()
+            layer(x).pow(2).sum().backward()
+            n_cap.append(len(algo._captured))
+            opt.step()
+            algo.step()
+        out[mode] = (host(layer._csr.col_indices), host(layer._csr.row_nnz),
+                     host(layer._csr.values), layer._csr.topology_version, n_cap)
+    a, b = out["every_step"], out["update_step"]
+    assert a[3] == b[3] > 0
+    assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+    assert bits_equal(a[2], b[2])
+    assert a[4] == [1] * 7 and b[4] == [0, 0, 1, 0, 0, 1, 0]
+
+
 def test_sparse_linear_init_matches_reference_draws():
     import sparsecore_b200 as sl
 
