@@ -231,12 +231,11 @@ class Workload:
                 self.algo = sl.SET(sparsity=cfg.ffn_sparsity, drop_fraction=cfg.drop_fraction,
                                    update_freq=cfg.update_freq, seed=0)
             else:
-                # Eager steps clone X / dY only on update steps (same topology
-                # as cloning every step); a replayed graph runs no hooks, so the
-                # clones must be recorded into it on every step.
+                # X / dY are cloned only before an update step (same topology as
+                # cloning every step); under --graph the step keeps one graph
+                # with the clones and one without.
                 self.algo = sl.RigL(sparsity=cfg.ffn_sparsity, drop_fraction=cfg.drop_fraction,
-                                    update_freq=cfg.update_freq, seed=0,
-                                    capture="every_step" if capturable else "update_step")
+                                    update_freq=cfg.update_freq, seed=0, capture="update_step")
             self.opt = torch.optim.AdamW(self.model.parameters(), lr=cfg.lr,
                                          capturable=capturable)
             nb = batch or cfg.batch
@@ -363,7 +362,8 @@ def run_ours(args, rank, world, local_rank):
     if args.graph:
         from sparsecore_b200.graph import GraphedStep
 
-        graphed = GraphedStep(model, train, batch_dev)
+        graphed = GraphedStep(model, train, batch_dev,
+                              variant=getattr(algo, "graph_variant", None))
 
         def step(batch):  # noqa: F811 - the graph reads the static batch_dev
             loss = graphed()

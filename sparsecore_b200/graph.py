@@ -20,6 +20,12 @@ here, returns the loss tensor, and contains no host synchronisation (no
 capturable=True)``; plain SGD is).  The step must have run eagerly at least
 once before the first capture (lazy library initialisation).  Router steps
 stay outside the graph.
+
+``variant`` (optional) is a callable returning a hashable key for steps
+whose recorded work differs: RigL with ``capture="update_step"`` clones its
+inputs only before an update, so ``variant=algo.graph_variant`` keeps two
+graphs, one with the clones and one without, and replays the one the next
+step needs.  All variants are dropped on a topology change.
 """
 from __future__ import annotations
 
@@ -33,38 +39,51 @@ __all__ = ["GraphedStep"]
 
 
 class GraphedStep:
-    def __init__(self, model: torch.nn.Module, step_fn, static_inputs: tuple):
+    def __init__(self, model: torch.nn.Module, step_fn, static_inputs: tuple, variant=None):
         self.model = model
         self.step_fn = step_fn
         self.inputs = tuple(static_inputs)
+        self.variant = variant
         self.layers = [m for m in model.modules() if isinstance(m, SparseLinear)]
+        self._graphs: dict = {}  # variant key -> (graph, loss, launches)
+        self._key = None
         self.graph: torch.cuda.CUDAGraph | None = None
         self.loss: torch.Tensor | None = None
-        self._key = None
         self.captures = 0
-        self.launches_per_replay = 0  # this library's kernels inside the graph
+        self.launches_per_replay = 0  # this library's kernels inside the last graph replayed
 
     def _topology(self):
         return tuple((id(m._csr), m._csr.topology_version) for m in self.layers)
 
+    def _variant(self):
+        return self.variant() if self.variant is not None else None
+
     def capture(self) -> None:
+        """Capture the step for the current variant (re-capturing all of them
+        from scratch if the topology changed)."""
+        if self._topology() != self._key:
+            self._graphs.clear()  # release the previous graphs' memory first
+            self.graph = None
         for m in self.layers:
             ops._cached_transpose(m._csr)  # rebuild (eagerly) before recording
         torch.cuda.synchronize()
-        self.graph = None  # release the previous graph's memory first
+        v = self._variant()
+        self._graphs.pop(v, None)
         g = torch.cuda.CUDAGraph()
         l0 = N.launches["count"]
         with torch.cuda.graph(g):
-            self.loss = self.step_fn(*self.inputs)
-        self.launches_per_replay = N.launches["count"] - l0
+            loss = self.step_fn(*self.inputs)
+        launches = N.launches["count"] - l0
         N.launches["count"] = l0
-        self.graph = g
+        self._graphs[v] = (g, loss, launches)
         self._key = self._topology()
         self.captures += 1
 
     def __call__(self) -> torch.Tensor:
-        if self.graph is None or self._topology() != self._key:
+        v = self._variant()
+        if self._topology() != self._key or v not in self._graphs:
             self.capture()
+        self.graph, self.loss, self.launches_per_replay = self._graphs[v]
         self.graph.replay()
         N.launches["count"] += self.launches_per_replay
         return self.loss

@@ -209,9 +209,16 @@ class RigL(DynamicSparsityAlgorithm):
         self._captured: dict[int, dict] = {}
         self._hook_handles: list = []
         self.capture = capture
+        self._generation = 0
 
     def _capturing(self) -> bool:
         return self.capture == "every_step" or (self._step_idx + 1) % self.update_freq == 0
+
+    def graph_variant(self):
+        """Key for a CUDA-graphed step: whether the next forward / backward
+        clones X and dY, and into which generation of clone buffers (an update
+        drops them, so a graph recorded before it must not be replayed after)."""
+        return (self._capturing(), self._generation if self._capturing() else 0)
 
     def attach(self, layer) -> None:
         before = len(self.layers)
@@ -232,6 +239,7 @@ class RigL(DynamicSparsityAlgorithm):
         self._hook_handles.append(layer.register_full_backward_hook(_bwd_hook))
 
     def update(self) -> None:
+        self._generation += 1
         for layer in self.layers:
             self._update_layer(layer, self._rng)
 

@@ -50,3 +50,59 @@ def test_graph_replay_matches_eager_across_topology_updates():
         algo2.step()
     assert graphed == eager
     assert gs.captures == 3  # initial + after the updates at steps 4 and 8
+
+
+def _setup_rigl(capture):
+    import sparsecore_b200 as sl
+
+    torch.manual_seed(0)
+    model = torch.nn.Sequential(sl.SparseLinear(64, 48, sparsity=0.8), torch.nn.ReLU(),
+                                sl.SparseLinear(48, 10, sparsity=0.7))
+    algo = sl.RigL(sparsity=0.8, drop_fraction=0.3, update_freq=3, seed=1, capture=capture)
+    model.apply(algo)
+    opt = torch.optim.SGD(model.parameters(), lr=0.05)
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(40, 64, generator=g).to(dev())
+    y = torch.randint(0, 10, (40,), generator=g).to(dev())
+
+    def train(xb, yb):
+        opt.zero_grad(set_to_none=True)
+        loss = torch.nn.functional.cross_entropy(model(xb), yb)
+        loss.backward()
+        opt.step()
+        return loss
+
+    return model, algo, train, x, y
+
+
+@pytest.mark.parametrize("capture", ["every_step", "update_step"])
+def test_graph_variants_for_rigl_capture(capture):
+    """RigL clones X / dY inside the graph: with capture="update_step" the
+    step keeps a graph with the clones and one without (keyed by
+    graph_variant), and replay matches eager every-step capture exactly."""
+    from sparsecore_b200.graph import GraphedStep
+
+    model, algo, train, x, y = _setup_rigl("every_step")
+    eager = []
+    for _ in range(10):
+        eager.append(float(train(x, y).item()))
+        algo.step()
+    ref_cols = [m._csr.col_indices.cpu() for m in model if hasattr(m, "_csr")]
+
+    model2, algo2, train2, x2, y2 = _setup_rigl(capture)
+    train2(x2, y2)
+    algo2.step()
+    gs = GraphedStep(model2, train2, (x2, y2), variant=algo2.graph_variant)
+    graphed = [eager[0]]
+    for _ in range(9):
+        graphed.append(float(gs().item()))
+        algo2.step()
+    assert graphed == eager
+    cols = [m._csr.col_indices.cpu() for m in model2 if hasattr(m, "_csr")]
+    assert all(torch.equal(a, b) for a, b in zip(ref_cols, cols))
+    assert model2[0]._csr.topology_version > 0
+    # Updates follow steps 2, 5 and 8.  every_step: one graph per topology /
+    # clone generation (captured at steps 1, 3, 6, 9); update_step: a
+    # clone-free graph per topology (1, 3, 6, 9) plus the cloning one before
+    # each update (2, 5, 8).
+    assert gs.captures == (4 if capture == "every_step" else 7)
