@@ -241,12 +241,15 @@ sddmm_lane_kernel(int M, int spr, int64_t N, const int32_t* __restrict__ row_sta
 // their 16 chains in registers for the whole sweep over N (quad layout as
 // above: quad lane q owns chains 4q..4q+3), so every operand element is
 // fetched from L2 once per tile instead of once per slot.  A tile holding
-// more than 512 slots sweeps N once per batch of 512.  Same rounding
+// more than 512 slots sweeps N once per batch of 512.  Within a batch the
+// slots are ordered so that the two quads of each quarter-warp read opposite
+// bank halves (see the batch-order comment in the kernel).  Same rounding
 // sequence as the other SDDMM kernels (N % 16 == 0: no 8-wide step, no tail).
 constexpr int kTThreads = 256;
 constexpr int kTQuads = kTThreads / 4;
 constexpr int kTS = 8;                    // slots per quad per batch
 constexpr int kTBatch = kTQuads * kTS;    // 512
+static_assert(kTBatch == 2 * kTThreads, "batch setup: two positions per consumer thread");
 constexpr int kTJ = 32;                   // columns per chunk: 128-byte rows
 constexpr int kTMaxRows = 128;
 constexpr int kTStages = 5;
@@ -263,6 +266,29 @@ __device__ __forceinline__ int lower_bound_cols(const int32_t* __restrict__ c, i
     return lo;
 }
 
+// Named barrier 1 over the kTThreads consumer threads (the producer warp
+// never joins it).
+__device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kTThreads) : "memory"); }
+
+// Exclusive scan over the kTThreads consumer threads.
+__device__ __forceinline__ int consumer_exclusive_scan(int v, int* ws, int* total) {
+    constexpr int NW = kTThreads / 32;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int inc = warp_inclusive_scan(v);
+    if (lane == 31) ws[warp] = inc;
+    consumer_bar();
+    if (warp == 0) {
+        int w = lane < NW ? ws[lane] : 0;
+        w = warp_inclusive_scan(w);
+        if (lane < NW) ws[lane] = w;
+    }
+    consumer_bar();
+    const int base = warp ? ws[warp - 1] : 0;
+    *total = ws[NW - 1];
+    consumer_bar();
+    return base + inc - v;
+}
+
 __global__ void __launch_bounds__(kTThreads + 32, 2)
 sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_constant__ CUtensorMap xmap,
                    int M, int64_t N, int TR, int TC, int n_bc,
@@ -276,7 +302,8 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
     __shared__ int run_lo[kTMaxRows];
     __shared__ int run_pref[kTMaxRows + 1];
     __shared__ int ws[(kTThreads + 32) / 32];
-    __shared__ int slot_of[kTBatch];  // global slot of each batch position (-1 = none)
+    __shared__ int ord_slot[kTBatch];  // batch position -> global slot (-1 = none)
+    __shared__ int ord_rc[kTBatch];    // (tile row << 16) | tile column
 
     const int tid = threadIdx.x, lane = tid & 31, q = lane & 3, quad = tid >> 2;
     const bool producer = tid >= kTThreads;  // warp 8 issues the copies
@@ -346,30 +373,70 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
         return;
     }
 
+    // A timed-out wait sets ok = false; the thread then skips further waits
+    // but still reaches every named barrier, so no consumer is left waiting.
+    bool ok = true;
     unsigned fph = 0u;  // bit b = parity of stage b's next fill
     for (int bt = 0; bt < nbatch; ++bt) {
+        // Batch order.  A warp-wide 128-bit shared load is served one
+        // quarter-warp (two quads) at a time, and a quad reads one 64-byte
+        // half of a swizzled 128-byte X row: banks 0-15 when (c & 4) == 0,
+        // banks 16-31 otherwise (the other half the opposite way).  The
+        // batch's slots (tile row-major order) are split by that bit into two
+        // lists and interleaved, so the two quads of a quarter-warp take one
+        // slot of each class and never share a bank; only the unmatched tail
+        // of the longer list pairs equal classes.  Each list keeps row order,
+        // so a quad's consecutive slots still share dY rows.
         const int b0 = bt * kTBatch;
-        // Per slot: swizzled float offsets of its dY row and X row for the
-        // chunk's first 16 columns (the second 16 are the same ^ 16), packed
-        // as (dY << 16) | X; `fresh` bit s = slot s starts a new W row.
-        int off[kTS];
-        unsigned fresh = 0u;
-        int prev_r = -1;
+        int sl2[2], rc2[2], cls2[2];
+        int packed = 0;
 #pragma unroll
-        for (int s = 0; s < kTS; ++s) {
-            const int t = b0 + quad * kTS + s;
-            int r = 0, c = 0, sl = -1;
+        for (int u = 0; u < 2; ++u) {
+            const int t = b0 + 2 * tid + u;
+            sl2[u] = -1; rc2[u] = 0; cls2[u] = -1;
             if (t < total) {
                 int lo = 0, hi = TR;  // last r with run_pref[r] <= t
                 while (hi - lo > 1) {
                     const int mid = (lo + hi) >> 1;
                     if (run_pref[mid] <= t) lo = mid; else hi = mid;
                 }
-                sl = run_lo[lo] + (t - run_pref[lo]);
-                r = lo;
-                c = __ldg(cols + sl) - c0;
+                sl2[u] = run_lo[lo] + (t - run_pref[lo]);
+                const int c = __ldg(cols + sl2[u]) - c0;
+                rc2[u] = (lo << 16) | c;
+                cls2[u] = (c >> 2) & 1;
+                packed += cls2[u] ? (1 << 16) : 1;
             }
-            if (q == 0) slot_of[quad * kTS + s] = sl;
+        }
+        int tot_packed;
+        const int exs = consumer_exclusive_scan(packed, ws, &tot_packed);
+        const int n0 = tot_packed & 0xffff, n1 = tot_packed >> 16, m = min(n0, n1);
+        int rank0 = exs & 0xffff, rank1 = exs >> 16;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int p = 2 * tid + u;
+            if (cls2[u] < 0) {
+                if (p >= n0 + n1) { ord_slot[p] = -1; ord_rc[p] = 0; }
+                continue;
+            }
+            const int i = cls2[u] ? rank1++ : rank0++;
+            const int dest = i < m ? 2 * i + cls2[u] : 2 * m + (i - m);
+            ord_slot[dest] = sl2[u];
+            ord_rc[dest] = rc2[u];
+        }
+        consumer_bar();
+
+        // Quad Q's slot s sits at position 16 * (Q >> 1) + 2 * s + (Q & 1).
+        // Per slot: swizzled float offsets of its dY row and X row for the
+        // chunk's first 16 columns (the second 16 are the same ^ 16), packed
+        // as (dY << 16) | X; `fresh` bit s = slot s starts a new W row.
+        const int qbase = 16 * (quad >> 1) + (quad & 1);
+        int off[kTS];
+        unsigned fresh = 0u;
+        int prev_r = -1;
+#pragma unroll
+        for (int s = 0; s < kTS; ++s) {
+            const int rc = ord_rc[qbase + 2 * s];
+            const int r = rc >> 16, c = rc & 0xffff;
             const int yo = r * kTJ + ((q ^ (r & 7)) << 2);
             const int xo = TR * kTJ + c * kTJ + ((q ^ (c & 7)) << 2);
             off[s] = (yo << 16) | xo;
@@ -382,7 +449,7 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
 
         for (int k = 0; k < nchunks; ++k) {
             const int b = (bt * nchunks + k) % kTStages;
-            if (!mbar_wait(&full[b], (fph >> b) & 1u, status)) return;  // bounded; status raised
+            if (ok && !mbar_wait(&full[b], (fph >> b) & 1u, status)) ok = false;  // bounded
             fph ^= 1u << b;
             const float* sb = sbase + b * stage;
             float4 d0 = make_float4(0.f, 0.f, 0.f, 0.f), d1 = d0;
@@ -405,12 +472,13 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
             const float4 o = shfl_xor4(acc[s], 2);
             if (q < 2) acc[s] = add4(acc[s], o);
             const float4 hi = shfl_xor4(acc[s], 1);
-            const int sl = q == 0 ? slot_of[quad * kTS + s] : -1;
+            const int sl = (q == 0 && ok) ? ord_slot[qbase + 2 * s] : -1;
             if (sl >= 0) {
                 const float4 s4 = add4(acc[s], hi);
                 dW[sl] = __fadd_rn(__fadd_rn(s4.x, s4.z), __fadd_rn(s4.y, s4.w));
             }
         }
+        consumer_bar();  // ord_* are rewritten by the next batch's setup
     }
 }
 
