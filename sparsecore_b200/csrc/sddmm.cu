@@ -482,6 +482,54 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
     }
 }
 
+// ── N = 1 ───────────────────────────────────────────────────────────────
+// With one column the reference's order reduces to dW = fma(dY, X, +0)
+// (all 16 chains and the 8-wide step are empty; the single term is the
+// FMA of the scalar tail onto the +0 horizontal sum), so the SDDMM is a
+// stream over the slot arrays: one warp per row writes the row's whole
+// capacity (live slots and zeroed padding) with coalesced loads of the
+// column indices and coalesced stores, four 32-slot strips in flight per
+// warp, X gathered through L1.
+__global__ void __launch_bounds__(256)
+sddmm_n1_kernel(int M, const int32_t* __restrict__ row_start, const int32_t* __restrict__ row_nnz,
+                const int32_t* __restrict__ row_capacity, const int32_t* __restrict__ cols,
+                const float* __restrict__ dY, const float* __restrict__ X, float* __restrict__ dW) {
+    const int lane = threadIdx.x & 31;
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < M; row += warps) {
+        const int rs = __ldg(row_start + row), nn = __ldg(row_nnz + row);
+        const int cp = __ldg(row_capacity + row);
+        const float dy = __ldg(dY + row);
+        for (int k0 = 0; k0 < cp; k0 += 128) {
+            int c[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int k = k0 + 32 * u + lane;
+                c[u] = k < nn ? __ldg(cols + rs + k) : -1;
+            }
+            float x[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) x[u] = c[u] >= 0 ? __ldg(X + c[u]) : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int k = k0 + 32 * u + lane;
+                if (k < cp) dW[rs + k] = c[u] >= 0 ? fmaf(dy, x[u], 0.0f) : 0.0f;
+            }
+        }
+    }
+}
+
+int launch_dw_n1(const sl_csr* W, const float* dY, const float* X, float* dW, cudaStream_t s) {
+    const int M = static_cast<int>(W->nrows);
+    int64_t blocks = (static_cast<int64_t>(M) + 7) / 8;
+    const int64_t max_blocks = static_cast<int64_t>(num_sms()) * 8;
+    if (blocks > max_blocks) blocks = max_blocks;
+    sddmm_n1_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        M, W->row_start, W->row_nnz, W->row_capacity, W->col_indices, dY, X, dW);
+    SL_RETURN_IF_LAUNCH_FAILED("sl_sddmm_dw (N = 1)");
+    return SL_OK;
+}
+
 // Returns -1 when the tiled path does not apply.
 int try_tiled(const sl_csr* W, const float* dY, const float* X, int64_t N, float* dW, cudaStream_t s) {
     const int64_t M = W->nrows, K = W->ncols;
@@ -571,6 +619,10 @@ extern "C" int sl_sddmm_dw(const sl_csr* W, const float* dY, const float* X, int
     if (N > 0 && (dY == nullptr || (W->ncols > 0 && X == nullptr)))
         return fail(SL_ERR_INVALID, "sl_sddmm_dw: NULL dense operand");
     cudaStream_t s = as_stream(stream);
+    if (N == 1 && W->ncols > 0) {  // SPARSECORE_B200_N1=warp keeps the per-slot kernel (tests)
+        const char* e = std::getenv("SPARSECORE_B200_N1");
+        if (e == nullptr || e[0] != 'w') return launch_dw_n1(W, dY, X, dW, s);
+    }
     if (!tiled_disabled() && W->ncols > 0) {
         const int rc = try_tiled(W, dY, X, N, dW, s);
         if (rc >= 0) return rc;

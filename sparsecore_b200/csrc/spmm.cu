@@ -339,6 +339,186 @@ spmm_rowwarp_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
     }
 }
 
+// ── N = 1: one lane per row ─────────────────────────────────────────────
+// With one dense column the bit-exact chain of a row is a single serial
+// FMA sequence, so the row is the unit of parallelism and a lane (not a
+// warp) owns it: the 32 lanes of a warp run 32 rows' chains side by side,
+// one SIMT FMA per slot for all of them (the warp-per-row kernel spends a
+// warp instruction or two per slot instead).  Each lane streams its own
+// row's (col, value) arrays into its own slice of shared memory with
+// 16-byte cp.async copies, kVStages stages of SEG 4-slot groups in flight;
+// a lane only reads what it copied itself, so a per-thread
+// cp.async.wait_group is the only synchronisation in the loop.  Copies
+// start at the row's start rounded down to 4 slots; the lane skips slots
+// outside [rs, rs + nnz).  X is staged in shared memory once per CTA
+// (K <= kVMaxKs) or gathered through L1.  Lane slices are SEG * 4 + 4
+// words apart, so the 8 lanes of a quarter-warp read distinct bank groups.
+// One warp per CTA; SEG = 16-byte groups per lane per stage (16 when there
+// are too few rows to give every SM two warps, so each warp keeps more
+// bytes in flight; 8 otherwise).
+constexpr int64_t kVMaxKs = 16384;  // largest K staged in shared memory
+template <int SEG, int kVStages>
+struct SpmvShape {
+    static constexpr int kStride = SEG * 4 + 4;  // words per lane slice (bank spread)
+    static constexpr int kStageWords = 32 * kStride;
+    static constexpr size_t kBytes = size_t(kVStages) * kStageWords * 4 * 2;  // cols + values
+};
+
+template <bool CA>
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* src, bool pred) {
+    if constexpr (CA)
+        asm volatile(
+            "{\n .reg .pred p;\n setp.ne.b32 p, %2, 0;\n"
+            " @p cp.async.ca.shared.global [%0], [%1], 16;\n}\n"
+            ::"r"(smem_addr(smem_dst)), "l"(src), "r"(static_cast<int>(pred))
+            : "memory");
+    else
+        asm volatile(
+            "{\n .reg .pred p;\n setp.ne.b32 p, %2, 0;\n"
+            " @p cp.async.cg.shared.global [%0], [%1], 16;\n}\n"
+            ::"r"(smem_addr(smem_dst)), "l"(src), "r"(static_cast<int>(pred))
+            : "memory");
+}
+__device__ __forceinline__ bool aligned16_dev(const void* p) {
+    return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int NPEND>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(NPEND) : "memory"); }
+
+template <bool KS, int SEG, bool CA, int kVStages>
+__global__ void __launch_bounds__(32)
+spmv_lane_kernel(int M, int64_t K, int64_t cap, const int32_t* __restrict__ row_start,
+                 const int32_t* __restrict__ row_nnz, const int32_t* __restrict__ cols,
+                 const float* __restrict__ vals, const float* __restrict__ X,
+                 float* __restrict__ Y) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    using S = SpmvShape<SEG, kVStages>;
+    const int lane = threadIdx.x;
+    int* cbase = reinterpret_cast<int*>(smem_raw);
+    float* vbase = reinterpret_cast<float*>(smem_raw + S::kBytes / 2);
+    float* xs = reinterpret_cast<float*>(smem_raw + S::kBytes);
+
+    const int row = blockIdx.x * 32 + lane;
+    const bool live = row < M;
+    const int rs = live ? __ldg(row_start + row) : 0;
+    const int nn = live ? __ldg(row_nnz + row) : 0;
+    const int a = rs & ~3;  // first copied slot
+    const int ngroups = nn > 0 ? (rs + nn - a + 3) >> 2 : 0;
+    // A last group that would read past the arrays' end is loaded directly.
+    const int tailg = (nn > 0 && a + 4 * static_cast<int64_t>(ngroups) > cap) ? ngroups - 1 : -1;
+    const int ncopy = tailg >= 0 ? ngroups - 1 : ngroups;
+    const int nst = __reduce_max_sync(0xffffffffu, (ngroups + SEG - 1) / SEG);
+
+    // Each lane copies its own row's groups (16 bytes per copy).
+    auto issue = [&](int st) {  // one commit group per stage, empty ones included
+        const int b = st % kVStages;
+#pragma unroll
+        for (int g = 0; g < SEG; ++g) {
+            const int gi = st * SEG + g;
+            const bool p = gi < ncopy;
+            const int64_t off = p ? a + 4 * static_cast<int64_t>(gi) : 0;
+            const int dw = b * S::kStageWords + lane * S::kStride + 4 * g;
+            cp_async16<CA>(cbase + dw, cols + off, p);
+            cp_async16<CA>(vbase + dw, vals + off, p);
+        }
+        cp_async_commit();
+    };
+    const bool xasync = KS && (K % 4 == 0) && aligned16_dev(X);
+    if (KS) {
+        if (xasync) {
+            for (int64_t k = 4 * lane; k < K; k += 128) cp_async16<false>(xs + k, X + k, true);
+        } else {
+            for (int64_t k = lane; k < K; k += 32) xs[k] = __ldg(X + k);
+        }
+    }
+    cp_async_commit();  // X (oldest group)
+#pragma unroll
+    for (int st = 0; st < kVStages - 1; ++st) issue(st);
+    cp_async_wait<kVStages - 1>();  // X has landed
+    __syncwarp();
+
+    float y = 0.0f;
+    const int* cb = cbase + lane * S::kStride;
+    const float* vb = vbase + lane * S::kStride;
+    for (int st = 0; st < nst; ++st) {
+        issue(st + kVStages - 1);      // refill the slot freed at st - 1
+        cp_async_wait<kVStages - 1>();  // stage st has landed (a lane reads only its own copies)
+        const int b = st % kVStages;
+        const int4* c4 = reinterpret_cast<const int4*>(cb + b * S::kStageWords);
+        const float4* v4 = reinterpret_cast<const float4*>(vb + b * S::kStageWords);
+        // Straight-line over the stage: every shared load (group and X
+        // gather, clamped to a valid address) is unconditional so they can
+        // all be in flight before the chain; only the FMA is predicated.
+#pragma unroll
+        for (int g = 0; g < SEG; ++g) {
+            const int gi = st * SEG + g;
+            const int64_t s0 = a + 4 * static_cast<int64_t>(gi);
+            int c[4];
+            float v[4];
+            if (gi == tailg) {
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const bool in = s0 + t < rs + nn;
+                    c[t] = in ? __ldg(cols + s0 + t) : 0;
+                    v[t] = in ? __ldg(vals + s0 + t) : 0.0f;
+                }
+            } else {
+                const int4 cc = c4[g];
+                const float4 vv = v4[g];
+                c[0] = cc.x; c[1] = cc.y; c[2] = cc.z; c[3] = cc.w;
+                v[0] = vv.x; v[1] = vv.y; v[2] = vv.z; v[3] = vv.w;
+            }
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const bool in = static_cast<unsigned>(static_cast<int>(s0) + t - rs) < static_cast<unsigned>(nn);
+                const int cc = in ? c[t] : 0;
+                const float x = KS ? xs[cc] : __ldg(X + cc);
+                if (in) y = fmaf(v[t], x, y);
+            }
+        }
+    }
+    cp_async_wait<0>();
+    if (live) Y[row] = y;
+}
+
+template <bool KS, int SEG, bool CA, int ST>
+int launch_spmv_cfg(const sl_csr* W, const float* X, int64_t K, float* Y, cudaStream_t s) {
+    const int M = static_cast<int>(W->nrows);
+    const size_t smem = SpmvShape<SEG, ST>::kBytes + (KS ? static_cast<size_t>(K) * 4 : 0);
+    auto kern = spmv_lane_kernel<KS, SEG, CA, ST>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+        return -1;
+    const int blocks = (M + 31) / 32;
+    kern<<<blocks, 32, smem, s>>>(M, K, W->total_capacity, W->row_start, W->row_nnz,
+                                  W->col_indices, W->values, X, Y);
+    SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd (N = 1)");
+    return SL_OK;
+}
+
+// Measured on B200 (4096 and 16384 rows x 4096 at 50-95%): with fewer warps
+// than two per SM, 16-group stages through L1 (cp.async.ca) keep the most
+// bytes in flight; with more, 8-group stages that bypass L1 (cp.async.cg),
+// so the many warps' rows do not evict each other.  Four stages, X in
+// shared memory, in both (deeper rings or X through L1 were slower).
+int launch_spmv(const sl_csr* W, const float* X, int64_t K, float* Y, cudaStream_t s) {
+    const int64_t warps = (W->nrows + 31) / 32;
+    const bool small = warps <= 2 * num_sms();
+    if (K <= kVMaxKs)
+        return small ? launch_spmv_cfg<true, 16, true, 4>(W, X, K, Y, s)
+                     : launch_spmv_cfg<true, 8, false, 4>(W, X, K, Y, s);
+    return small ? launch_spmv_cfg<false, 16, true, 4>(W, X, K, Y, s)
+                 : launch_spmv_cfg<false, 8, false, 4>(W, X, K, Y, s);
+}
+
+// SPARSECORE_B200_N1=warp keeps N = 1 on the warp-per-row kernel (tests).
+bool spmv_lane_enabled(const sl_csr* W) {
+    const char* e = std::getenv("SPARSECORE_B200_N1");
+    if (e != nullptr && e[0] == 'w') return false;
+    return aligned16(W->col_indices) && aligned16(W->values) && W->nrows > 0;
+}
+
 template <int CPL, bool N1, bool FULL = false>
 int launch_rowwarp(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_t s) {
     const int M = static_cast<int>(W->nrows);
@@ -593,6 +773,10 @@ extern "C" int sl_spmm_fwd(const sl_csr* W, const float* X, int64_t K, int64_t N
     const int path = fwd_path();
     if (path != kPathRows) {
         const int rc = try_xs(W, X, K, N, Y, s, path == kPathXs);
+        if (rc >= 0) return rc;
+    }
+    if (N == 1 && spmv_lane_enabled(W)) {
+        const int rc = launch_spmv(W, X, K, Y, s);
         if (rc >= 0) return rc;
     }
     if (N < 128) return dispatch_rowwarp(W, X, N, Y, s);

@@ -223,3 +223,41 @@ def test_tiled_sddmm_matches_slot_kernels_and_oracle(M, K, N, block, monkeypatch
     assert bits_equal(tiled, per_slot)
     assert bits_equal(tiled_quad, per_slot)
     assert bits_equal(tiled, O.sddmm(Wo, dY.numpy(), X.numpy()))
+
+
+@pytest.mark.parametrize("M,K,s,pr", [(70, 50, 0.5, 0.2), (9, 13, 0.0, 0.0), (129, 20000, 0.995, 0.2),
+                                      (300, 3000, 0.9, 0.0), (1000, 700, 0.97, 0.2),
+                                      (12000, 300, 0.9, 0.0)])
+def test_spmv_lane_kernel_matches_oracle_and_warp_kernel(M, K, s, pr, monkeypatch):
+    """N = 1: forward / dX on the lane-per-row kernel (cp.async row
+    segments) and the streaming SDDMM, against the oracle and the general
+    kernels: ragged and empty rows, rows whose 4-slot groups start unaligned
+    or run past the arrays' end (no padding), K above the shared-memory X
+    limit, one long row among short ones, and more rows than two warps per
+    SM (the second lane-kernel configuration)."""
+    import sparsecore_b200 as sl
+    from oracle import oracle as O
+    from sparsecore_b200 import ops
+
+    d = dev()
+    g = torch.Generator().manual_seed(M * 7 + K)
+    mask = torch.rand(M, K, generator=g) >= s
+    mask[min(3, M - 1)] = False  # an empty row
+    mask[M // 2, : min(K, 2500)] = True  # a long row
+    Wd = torch.randn(M, K, generator=g) * mask
+    W = sl.PaddedCSR.from_dense(Wd.to(d), padding_ratio=pr)
+    Wo = oracle_csr(W)
+    X = torch.randn(K, 1, generator=g)
+    dY = torch.randn(M, 1, generator=g)
+    WT, _ = sl.transpose_with_perm(W)
+    WTo, _ = O.transpose_with_perm(Wo)
+    y = sl.spmm(W, X.to(d))
+    dx = ops._spmm_raw(WT, dY.to(d))
+    dw = ops._sddmm_raw(W, dY.to(d), X.to(d))  # streaming N = 1 SDDMM
+    assert bits_equal(y, O.spmm(Wo, X.numpy()))
+    assert bits_equal(dx, O.spmm(WTo, dY.numpy()))
+    assert bits_equal(dw, O.sddmm(Wo, dY.numpy(), X.numpy()))
+    monkeypatch.setenv("SPARSECORE_B200_N1", "warp")
+    assert bits_equal(sl.spmm(W, X.to(d)), y)
+    assert bits_equal(ops._spmm_raw(WT, dY.to(d)), dx)
+    assert bits_equal(ops._sddmm_raw(W, dY.to(d), X.to(d)), dw)
