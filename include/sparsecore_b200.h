@@ -215,6 +215,21 @@ SL_API int sl_dst_apply_cols(const sl_csr* W, const float* thr_dev,
                       const int32_t* grow_offsets, const int32_t* grow_cols,
                       void* stream);
 
+/* SET regrow draws, on the host (no device work; host pointers).  For each
+ * row i with n_live[i] > 0, pool = ncols - n_keep[i], n_drop = n_live[i] -
+ * n_keep[i], and (when pool and n_drop are non-zero) n_grow = min(n_drop,
+ * pool) ranks drawn exactly as numpy's Generator(PCG64).choice(pool,
+ * size=n_grow, replace=False) called row by row (sparselab/router.py:457-470
+ * SET._update_layer); counts[i] = n_grow (0 otherwise) and the ranks are
+ * concatenated into ranks[0 .. *n_ranks).  Generator state in / out:
+ * pcg_state = {state_hi, state_lo, inc_hi, inc_lo}, *has_uint32, *uinteger
+ * (numpy's bit_generator.state fields).  SL_ERR_INVALID when ranks_cap is
+ * too small. */
+SL_API int sl_set_regrow_draws(uint64_t* pcg_state, int32_t* has_uint32, uint32_t* uinteger,
+                        int64_t nrows, const int32_t* n_live, const int32_t* n_keep,
+                        int64_t ncols, int32_t* counts, int32_t* ranks, int64_t ranks_cap,
+                        int64_t* n_ranks);
+
 /* ── Dense layout helper ──────────────────────────────────────────────────
  * dst[cols, rows] = src[rows, cols]^T (fp32, row-major, not in place).
  * Replaces the torch copies of the reference's SparseLinear

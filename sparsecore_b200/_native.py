@@ -69,6 +69,7 @@ SIGNATURES: dict[str, tuple] = {
     "sl_unpack_live": (I32, [P, P, P, P, F32, P]),
     "sl_exclusive_scan": (I32, [P, I64, P, P, P]),
     "sl_transpose_f32": (I32, [P, I64, I64, P, P]),
+    "sl_set_regrow_draws": (I32, [P, P, P, I64, P, P, I64, P, P, I64, P]),
 }
 
 _lib = None
@@ -129,6 +130,7 @@ KERNELS_PER_CALL = {
     "sl_to_dense": 1, "sl_check_invariants": 2, "sl_dense_grad": 1, "sl_dst_threshold": 9,
     "sl_dst_keep": 1, "sl_dst_apply_random": 1, "sl_dst_apply_topk": 1, "sl_dst_apply_cols": 1,
     "sl_pack_live": 1, "sl_unpack_live": 1, "sl_exclusive_scan": 1,
+    "sl_set_regrow_draws": 0,  # host only
 }
 launches = {"count": 0}
 

@@ -30,6 +30,8 @@ from __future__ import annotations
 
 from typing import TYPE_CHECKING
 
+import ctypes
+
 import numpy as np
 import torch
 
@@ -147,6 +149,52 @@ def _check_cols(csr) -> None:
                            f"of {int(N.lib().sl_dst_max_ncols())}")
 
 
+def _regrow_draws(rng: np.random.Generator, n_live: np.ndarray, n_keep: np.ndarray,
+                  ncols: int) -> tuple[np.ndarray, np.ndarray]:
+    """Per-row SET regrow ranks, as the reference's loop of
+    ``rng.choice(pool, size=n_grow, replace=False)`` over the live rows
+    (sparselab/router.py:457-470) draws them, and with ``rng`` advanced to
+    the same state afterwards.  A PCG64 generator (``default_rng``) runs in
+    ``sl_set_regrow_draws``; any other bit generator takes the per-row loop.
+    Returns (counts[int32, nrows], ranks[int32, sum(counts)])."""
+    n_live = np.ascontiguousarray(n_live, dtype=np.int32)
+    n_keep = np.ascontiguousarray(n_keep, dtype=np.int32)
+    nrows = n_live.shape[0]
+    st = rng.bit_generator.state
+    if st.get("bit_generator") != "PCG64":
+        counts = np.zeros(nrows, np.int32)
+        draws = []
+        for i in np.nonzero(n_live)[0]:
+            nk = int(n_keep[i])
+            n_drop, pool = int(n_live[i]) - nk, ncols - nk
+            if pool == 0 or n_drop == 0:
+                continue
+            n_grow = min(n_drop, pool)
+            draws.append(rng.choice(pool, size=n_grow, replace=False))
+            counts[i] = n_grow
+        ranks = np.concatenate(draws).astype(np.int32) if draws else np.zeros(0, np.int32)
+        return counts, ranks
+    m64 = (1 << 64) - 1
+    s128, inc = int(st["state"]["state"]), int(st["state"]["inc"])
+    pcg = np.array([s128 >> 64, s128 & m64, inc >> 64, inc & m64], dtype=np.uint64)
+    has32 = np.array([int(st["has_uint32"])], dtype=np.int32)
+    u32 = np.array([int(st["uinteger"])], dtype=np.uint32)
+    counts = np.zeros(nrows, np.int32)
+    cap = int(np.maximum(n_live.astype(np.int64) - n_keep, 0).sum())
+    ranks = np.zeros(max(cap, 1), np.int32)
+    n_ranks = np.zeros(1, np.int64)
+    c = ctypes
+    N.call("sl_set_regrow_draws", pcg.ctypes.data_as(c.c_void_p), has32.ctypes.data_as(c.c_void_p),
+           u32.ctypes.data_as(c.c_void_p), nrows, n_live.ctypes.data_as(c.c_void_p),
+           n_keep.ctypes.data_as(c.c_void_p), ncols, counts.ctypes.data_as(c.c_void_p),
+           ranks.ctypes.data_as(c.c_void_p), cap, n_ranks.ctypes.data_as(c.c_void_p))
+    st["state"]["state"] = (int(pcg[0]) << 64) | int(pcg[1])
+    st["has_uint32"] = int(has32[0])
+    st["uinteger"] = int(u32[0])
+    rng.bit_generator.state = st
+    return counts, ranks[: int(n_ranks[0])]
+
+
 class SET(DynamicSparsityAlgorithm):
     """Sparse Evolutionary Training (Mocanu et al. 2018): global magnitude
     prune, random regrow at zero (router.py:296-483)."""
@@ -166,23 +214,11 @@ class SET(DynamicSparsityAlgorithm):
             return
         _check_cols(csr)
         pr = _Prune(csr, self.drop_fraction)
-        n_live = csr._rn_h
-        n_keep = pr.n_keep.cpu().numpy()
-        ncols = csr.ncols
-        counts = np.zeros(csr.nrows, np.int32)
-        draws = []
-        for i in np.nonzero(n_live)[0]:
-            nk = int(n_keep[i])
-            n_drop = int(n_live[i]) - nk
-            pool = ncols - nk
-            if pool == 0 or n_drop == 0:
-                continue
-            n_grow = min(n_drop, pool)
-            draws.append(rng.choice(pool, size=n_grow, replace=False))
-            counts[i] = n_grow
+        counts, ranks = _regrow_draws(rng, csr._rn_h, pr.n_keep.cpu().numpy(), csr.ncols)
         off = np.zeros(csr.nrows + 1, np.int32)
         np.cumsum(counts, out=off[1:])
-        ranks = (np.concatenate(draws).astype(np.int32) if draws else np.zeros(1, np.int32))
+        if ranks.size == 0:
+            ranks = np.zeros(1, np.int32)
         dev = csr.device
         off_d = torch.from_numpy(off).to(dev)
         ranks_d = torch.from_numpy(ranks).to(dev)

@@ -90,6 +90,26 @@ def test_router_and_dp_validation(lib):
     assert lib.sl_dense_grad(BAD, None, 2, 2, 2, BAD, None) == N.SL_ERR_INVALID
     assert lib.sl_pack_live(ref(csr()), None, BAD, BAD, None) == N.SL_ERR_INVALID
     assert lib.sl_unpack_live(ref(csr()), BAD, None, BAD, 1.0, None) == N.SL_ERR_INVALID
+    # host-only SET draws: NULL state / arrays, survivors out of range, short buffer
+    import numpy as np
+
+    st = np.zeros(4, np.uint64)
+    h32 = np.zeros(1, np.int32)
+    u32 = np.zeros(1, np.uint32)
+    live, keep = np.array([5], np.int32), np.array([6], np.int32)
+    cnt, rk, nr = np.zeros(1, np.int32), np.zeros(4, np.int32), np.zeros(1, np.int64)
+    a = lambda x: x.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+    assert lib.sl_set_regrow_draws(None, a(h32), a(u32), 1, a(live), a(keep), 10, a(cnt), a(rk), 4,
+                                   a(nr)) == N.SL_ERR_INVALID
+    assert lib.sl_set_regrow_draws(a(st), a(h32), a(u32), 1, None, a(keep), 10, a(cnt), a(rk), 4,
+                                   a(nr)) == N.SL_ERR_INVALID
+    assert lib.sl_set_regrow_draws(a(st), a(h32), a(u32), 1, a(live), a(keep), 10, a(cnt), a(rk), 4,
+                                   a(nr)) == N.SL_ERR_INVALID
+    assert "survivors out of range" in err(lib)
+    keep[0] = 1
+    assert lib.sl_set_regrow_draws(a(st), a(h32), a(u32), 1, a(live), a(keep), 10, a(cnt), a(rk), 3,
+                                   a(nr)) == N.SL_ERR_INVALID
+    assert "too small" in err(lib)
 
 
 def test_python_layer_maps_codes_to_reference_exceptions(lib):
