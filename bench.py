@@ -430,7 +430,13 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     e2e_ms = (time.perf_counter() - w0) * 1e3
 
-    # one router update + topology broadcast, timed on its own
+    # one router update + topology broadcast, timed on its own.  RigL needs
+    # the captured X / dY of a step first (with capture="update_step" only an
+    # update step records them): run one capturing step outside the timing.
+    if getattr(algo, "capture", None) == "update_step":
+        algo.capture = "every_step"
+        train(*batch_dev)
+        algo.capture = "update_step"
     barrier()
     r0 = time.perf_counter()
     algo.update()
