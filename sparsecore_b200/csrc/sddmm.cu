@@ -291,7 +291,7 @@ __device__ __forceinline__ int consumer_exclusive_scan(int v, int* ws, int* tota
 
 __global__ void __launch_bounds__(kTThreads + 32, 2)
 sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_constant__ CUtensorMap xmap,
-                   int M, int64_t N, int TR, int TC, int n_bc,
+                   int M, int64_t N, int TR, int TC, int n_bc, int n_bi, int col_major,
                    const int32_t* __restrict__ row_start, const int32_t* __restrict__ row_nnz,
                    const int32_t* __restrict__ row_capacity, const int32_t* __restrict__ cols,
                    float* __restrict__ dW, unsigned* status) {
@@ -307,7 +307,11 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
 
     const int tid = threadIdx.x, lane = tid & 31, q = lane & 3, quad = tid >> 2;
     const bool producer = tid >= kTThreads;  // warp 8 issues the copies
-    const int bi = blockIdx.x / n_bc, bc = blockIdx.x % n_bc;
+    // Tile order: CTAs resident together share the larger operand's tile
+    // (col_major: the same X column tile, row tiles fastest), so it is read
+    // from DRAM about once and the smaller operand stays in L2.
+    const int bi = col_major ? static_cast<int>(blockIdx.x % n_bi) : static_cast<int>(blockIdx.x / n_bc);
+    const int bc = col_major ? static_cast<int>(blockIdx.x / n_bi) : static_cast<int>(blockIdx.x % n_bc);
     const int r0 = bi * TR, c0 = bc * TC;
     const int nrows = min(TR, M - r0);
 
@@ -560,9 +564,12 @@ int try_tiled(const sl_csr* W, const float* dY, const float* X, int64_t N, float
                              static_cast<int>(smem)) != cudaSuccess)
         return -1;
     const int n_bi = static_cast<int>((M + TR - 1) / TR), n_bc = static_cast<int>((K + TC - 1) / TC);
+    int col_major = K > M ? 1 : 0;  // X (K x N) is the larger operand
+    if (const char* e = std::getenv("SPARSECORE_B200_DW_ORDER"))  // row|col (measurements)
+        col_major = e[0] == 'c' ? 1 : 0;
     kern<<<n_bi * n_bc, kTThreads + 32, smem, s>>>(
-        dymap, xmap, static_cast<int>(M), N, TR, TC, n_bc, W->row_start, W->row_nnz,
-        W->row_capacity, W->col_indices, dW, status);
+        dymap, xmap, static_cast<int>(M), N, TR, TC, n_bc, n_bi, col_major, W->row_start,
+        W->row_nnz, W->row_capacity, W->col_indices, dW, status);
     SL_RETURN_IF_LAUNCH_FAILED("sl_sddmm_dw (tiled)");
     return SL_OK;
 }

@@ -216,12 +216,13 @@ def test_tiled_sddmm_matches_slot_kernels_and_oracle(M, K, N, block, monkeypatch
     WTo, _ = O.transpose_with_perm(Wo)
     assert bits_equal(ops._spmm_raw(WT, dY.to(d)), O.spmm(WTo, dY.numpy()))
     tiled = ops._sddmm_raw(W, dY.to(d), X.to(d))  # paired-slot lane mapping
-    monkeypatch.setenv("SPARSECORE_B200_DW_MAP", "quad")
-    tiled_quad = ops._sddmm_raw(W, dY.to(d), X.to(d))
+    other = "row" if K > M else "col"  # the tile order the default did not take
+    monkeypatch.setenv("SPARSECORE_B200_DW_ORDER", other)
+    tiled_other = ops._sddmm_raw(W, dY.to(d), X.to(d))
     monkeypatch.setenv("SPARSECORE_B200_DW", "quad")
     per_slot = ops._sddmm_raw(W, dY.to(d), X.to(d))
     assert bits_equal(tiled, per_slot)
-    assert bits_equal(tiled_quad, per_slot)
+    assert bits_equal(tiled_other, per_slot)
     assert bits_equal(tiled, O.sddmm(Wo, dY.numpy(), X.numpy()))
 
 
