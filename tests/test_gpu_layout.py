@@ -173,6 +173,7 @@ def test_dense_transpose_kernel_exact():
     from sparsecore_b200 import ops
 
     g = torch.Generator().manual_seed(5)
-    for r, c in [(1, 1), (33, 65), (1000, 7), (7, 1000), (512, 3072)]:
+    # scalar path (odd shapes) and the 64 x 64 float4 path, whole and partial tiles
+    for r, c in [(1, 1), (33, 65), (1000, 7), (7, 1000), (512, 3072), (68, 132), (4, 200), (260, 4)]:
         a = torch.randn(r, c, generator=g).cuda()
         assert torch.equal(ops._transpose(a), a.t().contiguous()), (r, c)
