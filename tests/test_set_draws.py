@@ -69,3 +69,16 @@ def test_tail_shuffle_path_is_taken_and_matches():
     _, got = _regrow_draws(b, n_live, n_keep, 20000)
     assert np.array_equal(got, want.astype(np.int32))
     assert b.bit_generator.state == a.bit_generator.state
+
+
+def test_non_pcg64_generator_takes_the_per_row_loop():
+    from sparsecore_b200.router import _regrow_draws
+
+    n_live = np.array([10, 0, 7, 5], np.int32)
+    n_keep = np.array([6, 0, 7, 1], np.int32)
+    a = np.random.Generator(np.random.MT19937(3))
+    b = np.random.Generator(np.random.MT19937(3))
+    want = _reference_loop(a, n_live, n_keep, 40)
+    got = _regrow_draws(b, n_live, n_keep, 40)
+    assert np.array_equal(got[0], want[0]) and np.array_equal(got[1], want[1])
+    assert b.random() == a.random()
