@@ -512,6 +512,138 @@ int launch_spmv(const sl_csr* W, const float* X, int64_t K, float* Y, cudaStream
                  : launch_spmv_cfg<false, 8, false, 4>(W, X, K, Y, s);
 }
 
+// ── N = 4 or 8: one lane per row ─────────────────────────────────────────
+// The N = 1 scheme with N / 4 float4 columns per lane: lane = row, its
+// (col, value) stream staged by per-lane cp.async exactly as above, and per
+// slot the lane gathers its X row (NV 16-byte loads through L1) and updates
+// its 4 * NV column accumulators, each in slot order (the reference's chain
+// per output element).  A warp advances 32 rows by one slot with NV loads
+// and 4 * NV FMAs, where the warp-per-row kernel spends several warp
+// instructions and a dependent shared round trip per slot.
+template <int NV>
+__global__ void __launch_bounds__(32)
+spmm_lanerow_kernel(int M, int64_t cap, const int32_t* __restrict__ row_start,
+                    const int32_t* __restrict__ row_nnz, const int32_t* __restrict__ cols,
+                    const float* __restrict__ vals, const float* __restrict__ X,
+                    float* __restrict__ Y) {
+    constexpr int SEG = 8, ST = 4;
+    constexpr int N = 4 * NV;
+    using S = SpmvShape<SEG, ST>;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int lane = threadIdx.x;
+    int* cbase = reinterpret_cast<int*>(smem_raw);
+    float* vbase = reinterpret_cast<float*>(smem_raw + S::kBytes / 2);
+    const int row = blockIdx.x * 32 + lane;
+    const bool live = row < M;
+    const int rs = live ? __ldg(row_start + row) : 0;
+    const int nn = live ? __ldg(row_nnz + row) : 0;
+    const int a = rs & ~3;
+    const int ngroups = nn > 0 ? (rs + nn - a + 3) >> 2 : 0;
+    const int tailg = (nn > 0 && a + 4 * static_cast<int64_t>(ngroups) > cap) ? ngroups - 1 : -1;
+    const int ncopy = tailg >= 0 ? ngroups - 1 : ngroups;
+    const int nst = __reduce_max_sync(0xffffffffu, (ngroups + SEG - 1) / SEG);
+    auto issue = [&](int st) {
+        const int b = st % ST;
+#pragma unroll
+        for (int g = 0; g < SEG; ++g) {
+            const int gi = st * SEG + g;
+            const bool p = gi < ncopy;
+            const int64_t off = p ? a + 4 * static_cast<int64_t>(gi) : 0;
+            const int dw = b * S::kStageWords + lane * S::kStride + 4 * g;
+            cp_async16<false>(cbase + dw, cols + off, p);
+            cp_async16<false>(vbase + dw, vals + off, p);
+        }
+        cp_async_commit();
+    };
+#pragma unroll
+    for (int st = 0; st < ST - 1; ++st) issue(st);
+
+    float4 acc[NV];
+#pragma unroll
+    for (int q = 0; q < NV; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int* cb = cbase + lane * S::kStride;
+    const float* vb = vbase + lane * S::kStride;
+    for (int st = 0; st < nst; ++st) {
+        issue(st + ST - 1);
+        cp_async_wait<ST - 1>();
+        const int b = st % ST;
+        const int4* c4 = reinterpret_cast<const int4*>(cb + b * S::kStageWords);
+        const float4* v4 = reinterpret_cast<const float4*>(vb + b * S::kStageWords);
+#pragma unroll 2
+        for (int g = 0; g < SEG; ++g) {
+            const int gi = st * SEG + g;
+            const int64_t s0 = a + 4 * static_cast<int64_t>(gi);
+            int c[4];
+            float v[4];
+            if (gi == tailg) {
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const bool in = s0 + t < rs + nn;
+                    c[t] = in ? __ldg(cols + s0 + t) : 0;
+                    v[t] = in ? __ldg(vals + s0 + t) : 0.0f;
+                }
+            } else {
+                const int4 cc = c4[g];
+                const float4 vv = v4[g];
+                c[0] = cc.x; c[1] = cc.y; c[2] = cc.z; c[3] = cc.w;
+                v[0] = vv.x; v[1] = vv.y; v[2] = vv.z; v[3] = vv.w;
+            }
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const bool in = static_cast<unsigned>(static_cast<int>(s0) + t - rs) < static_cast<unsigned>(nn);
+                const float4* xr = reinterpret_cast<const float4*>(X + static_cast<int64_t>(in ? c[t] : 0) * N);
+                float4 x[NV];
+#pragma unroll
+                for (int q = 0; q < NV; ++q) x[q] = __ldg(xr + q);
+                if (in) {
+#pragma unroll
+                    for (int q = 0; q < NV; ++q) {
+                        acc[q].x = fmaf(v[t], x[q].x, acc[q].x);
+                        acc[q].y = fmaf(v[t], x[q].y, acc[q].y);
+                        acc[q].z = fmaf(v[t], x[q].z, acc[q].z);
+                        acc[q].w = fmaf(v[t], x[q].w, acc[q].w);
+                    }
+                }
+            }
+        }
+    }
+    cp_async_wait<0>();
+    if (live) {
+        float4* yr = reinterpret_cast<float4*>(Y + static_cast<int64_t>(row) * N);
+#pragma unroll
+        for (int q = 0; q < NV; ++q) yr[q] = acc[q];
+    }
+}
+
+template <int NV>
+int launch_lanerow_nv(const sl_csr* W, const float* X, float* Y, cudaStream_t s) {
+    const size_t smem = SpmvShape<8, 4>::kBytes;
+    if (cudaFuncSetAttribute(spmm_lanerow_kernel<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+        return -1;
+    const int M = static_cast<int>(W->nrows);
+    spmm_lanerow_kernel<NV><<<(M + 31) / 32, 32, smem, s>>>(M, W->total_capacity, W->row_start,
+                                                             W->row_nnz, W->col_indices, W->values, X, Y);
+    SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd (lane per row)");
+    return SL_OK;
+}
+
+// Returns -1 when the lane-per-row path does not apply.  Measured on B200
+// (4096 and 16384 rows x 4096, 50-99%): it wins only for N <= 8 with at
+// least three warps of rows per SM (16384 x 4096, N = 8: 225 vs 458 us at
+// 50%); with fewer rows, or N = 32 (a 128-byte X row per lane per slot
+// through L1), the warp-per-row kernel is faster.
+// SPARSECORE_B200_SMALLN=warp|lane forces one of the two (tests).
+int try_lanerow(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_t s) {
+    if (N < 4 || N > 8 || N % 4 != 0 || !aligned16(X) || !aligned16(Y) ||
+        !aligned16(W->col_indices) || !aligned16(W->values) || W->nrows == 0)
+        return -1;
+    bool use = W->nrows >= static_cast<int64_t>(3) * 32 * num_sms();
+    if (const char* e = std::getenv("SPARSECORE_B200_SMALLN")) use = e[0] == 'l';
+    if (!use) return -1;
+    return N == 4 ? launch_lanerow_nv<1>(W, X, Y, s) : launch_lanerow_nv<2>(W, X, Y, s);
+}
+
 // SPARSECORE_B200_N1=warp keeps N = 1 on the warp-per-row kernel (tests).
 bool spmv_lane_enabled(const sl_csr* W) {
     const char* e = std::getenv("SPARSECORE_B200_N1");
@@ -777,6 +909,10 @@ extern "C" int sl_spmm_fwd(const sl_csr* W, const float* X, int64_t K, int64_t N
     }
     if (N == 1 && spmv_lane_enabled(W)) {
         const int rc = launch_spmv(W, X, K, Y, s);
+        if (rc >= 0) return rc;
+    }
+    if (N == 4 || N == 8) {
+        const int rc = try_lanerow(W, X, N, Y, s);
         if (rc >= 0) return rc;
     }
     if (N < 128) return dispatch_rowwarp(W, X, N, Y, s);

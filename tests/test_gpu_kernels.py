@@ -262,3 +262,37 @@ def test_spmv_lane_kernel_matches_oracle_and_warp_kernel(M, K, s, pr, monkeypatc
     assert bits_equal(sl.spmm(W, X.to(d)), y)
     assert bits_equal(ops._spmm_raw(WT, dY.to(d)), dx)
     assert bits_equal(ops._sddmm_raw(W, dY.to(d), X.to(d)), dw)
+
+
+@pytest.mark.parametrize("M,K,s,pr", [(70, 50, 0.5, 0.2), (9, 13, 0.0, 0.0), (300, 3000, 0.9, 0.0),
+                                      (1000, 700, 0.97, 0.2), (2000, 300, 0.8, 0.2)])
+def test_lanerow_small_n_matches_oracle_and_warp_kernel(M, K, s, pr, monkeypatch):
+    """N = 4 and 8: forward / dX on the lane-per-row kernel (one lane per
+    row, N column chains per lane; forced here, by default it runs only with
+    many rows) against the oracle and the warp-per-row kernel: ragged and empty rows, no padding (the last group
+    read past the arrays' end), one long row among short ones."""
+    import sparsecore_b200 as sl
+    from oracle import oracle as O
+    from sparsecore_b200 import ops
+
+    d = dev()
+    g = torch.Generator().manual_seed(M * 5 + K)
+    mask = torch.rand(M, K, generator=g) >= s
+    mask[min(3, M - 1)] = False
+    mask[M // 2, : min(K, 2500)] = True
+    W = sl.PaddedCSR.from_dense((torch.randn(M, K, generator=g) * mask).to(d), padding_ratio=pr)
+    Wo = oracle_csr(W)
+    WT, _ = sl.transpose_with_perm(W)
+    WTo, _ = O.transpose_with_perm(Wo)
+    for N in (4, 8):
+        X = torch.randn(K, N, generator=g)
+        dY = torch.randn(M, N, generator=g)
+        monkeypatch.setenv("SPARSECORE_B200_SMALLN", "lane")
+        y = sl.spmm(W, X.to(d))
+        dx = ops._spmm_raw(WT, dY.to(d))
+        assert bits_equal(y, O.spmm(Wo, X.numpy())), N
+        assert bits_equal(dx, O.spmm(WTo, dY.numpy())), N
+        monkeypatch.setenv("SPARSECORE_B200_SMALLN", "warp")
+        assert bits_equal(sl.spmm(W, X.to(d)), y), N
+        assert bits_equal(ops._spmm_raw(WT, dY.to(d)), dx), N
+        monkeypatch.delenv("SPARSECORE_B200_SMALLN")
