@@ -822,6 +822,12 @@ spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
     }
 }
 
+// Whether a K x 64 tile (TMA boxes of 128 rows) fits next to the staging.
+bool xs_lanes_for64(int64_t K) {
+    const int64_t rows = (K + kXsBoxRows - 1) / kXsBoxRows * kXsBoxRows;
+    return rows * 64 * 4 <= 200 * 1024;
+}
+
 // Tile width by K so that the resident tile fits in shared memory.
 int xs_lanes_for(int64_t K) {
     const int64_t rows = (K + kXsBoxRows - 1) / kXsBoxRows * kXsBoxRows;
@@ -879,7 +885,19 @@ int try_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, cuda
     // Measured on B200 (config-5 shapes, N = 16384): the X-stationary kernel
     // beats the row-gather kernel by 5-15% for K <= 1536 when M >= 1536
     // (many rows per resident tile); elsewhere the row-gather kernel wins.
-    if (xs_lanes_for(K) == 8 && (forced || W->nrows >= 1536)) return launch_xs<8>(W, X, K, N, Y, s);
+    if (!forced && W->nrows < 1536) return -1;
+    // Tile width: 64 columns (16 lanes per row: each staged (col, value)
+    // pair feeds 64 FMAs) where the K x 64 tile fits, measured 6% faster on
+    // the config-5 K = 768 layers and 21% on config-4 K = 384; else 32.
+    // Tuning knob SPARSECORE_B200_XS_TN=32|64.
+    int tn = xs_lanes_for64(K) ? 64 : (xs_lanes_for(K) == 8 ? 32 : 0);
+    if (const char* e = std::getenv("SPARSECORE_B200_XS_TN")) {
+        const int v = std::atoi(e);
+        if (v == 32 && xs_lanes_for(K) == 8) tn = 32;
+        if (v == 64 && xs_lanes_for64(K)) tn = 64;
+    }
+    if (tn == 64) return launch_xs<16>(W, X, K, N, Y, s);
+    if (tn == 32) return launch_xs<8>(W, X, K, N, Y, s);
     return -1;
 }
 }  // namespace
