@@ -882,10 +882,11 @@ int fwd_path() {
 int try_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, cudaStream_t s,
            bool forced) {
     if (N < 256 || N % 4 != 0 || !aligned16(X) || !aligned16(Y) || K < 1 || K > INT_MAX) return -1;
-    // Measured on B200 (config-5 shapes, N = 16384): the X-stationary kernel
-    // beats the row-gather kernel by 5-15% for K <= 1536 when M >= 1536
-    // (many rows per resident tile); elsewhere the row-gather kernel wins.
-    if (!forced && W->nrows < 1536) return -1;
+    // Measured on B200 (config-4/5 shapes, N = 16384): with 64-column tiles
+    // (K <= 768) the X-stationary kernel beats the row-gather kernel on every
+    // layer (384 to 3072 rows, 1-12%); with 32-column tiles only when
+    // M >= 1536 (many rows per resident tile).
+    if (!forced && W->nrows < 1536 && !xs_lanes_for64(K)) return -1;
     // Tile width: 64 columns (16 lanes per row: each staged (col, value)
     // pair feeds 64 FMAs) where the K x 64 tile fits, measured 6% faster on
     // the config-5 K = 768 layers and 21% on config-4 K = 384; else 32.
