@@ -721,7 +721,10 @@ int dispatch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStrea
 constexpr int kXsThreads = 512;
 constexpr int kXsWarps = kXsThreads / 32;
 constexpr int kXsBoxRows = 128;
-constexpr int kXsCh = 16;  // staged slots per row per chunk (TN = 32: 4 rows per warp)
+// Staged slots per row per chunk: 16, or 32 with one row per warp (TN = 128)
+// so that a chunk still fills whole warp-wide loads.
+template <int LPR>
+__host__ __device__ constexpr int xs_ch() { return LPR == 32 ? 32 : 16; }
 constexpr int kXsRowsPerItemMul = 4;
 
 template <int LPR>
@@ -741,6 +744,7 @@ spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane / LPR, li = lane % LPR;
+    constexpr int kXsCh = xs_ch<LPR>();
     constexpr int XST = kXsCh + 2;  // 16-byte aligned rows: two pairs per 128-bit read
     int2* st = stage + warp * RPW * XST;
     const int2* my = st + g * XST;
@@ -822,6 +826,11 @@ spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
     }
 }
 
+bool xs_lanes_for128(int64_t K) {
+    const int64_t rows = (K + kXsBoxRows - 1) / kXsBoxRows * kXsBoxRows;
+    return rows * 128 * 4 <= 200 * 1024;
+}
+
 // Whether a K x 64 tile (TMA boxes of 128 rows) fits next to the staging.
 bool xs_lanes_for64(int64_t K) {
     const int64_t rows = (K + kXsBoxRows - 1) / kXsBoxRows * kXsBoxRows;
@@ -849,7 +858,7 @@ int launch_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, c
     const int M = static_cast<int>(W->nrows);
     const int nbox = static_cast<int>((K + kXsBoxRows - 1) / kXsBoxRows);
     const size_t smem = static_cast<size_t>(nbox) * kXsBoxRows * TN * 4 +
-                        static_cast<size_t>(kXsWarps) * RPW * (kXsCh + 2) * sizeof(int2);
+                        static_cast<size_t>(kXsWarps) * RPW * (xs_ch<LPR>() + 2) * sizeof(int2);
     if (cudaFuncSetAttribute(spmm_xs_kernel<LPR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
         return -1;
@@ -887,16 +896,19 @@ int try_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, cuda
     // layer (384 to 3072 rows, 1-12%); with 32-column tiles only when
     // M >= 1536 (many rows per resident tile).
     if (!forced && W->nrows < 1536 && !xs_lanes_for64(K)) return -1;
-    // Tile width: 64 columns (16 lanes per row: each staged (col, value)
-    // pair feeds 64 FMAs) where the K x 64 tile fits, measured 6% faster on
-    // the config-5 K = 768 layers and 21% on config-4 K = 384; else 32.
-    // Tuning knob SPARSECORE_B200_XS_TN=32|64.
-    int tn = xs_lanes_for64(K) ? 64 : (xs_lanes_for(K) == 8 ? 32 : 0);
+    // Tile width: the widest of 128 / 64 / 32 columns whose K x TN tile fits
+    // (each staged (col, value) pair feeds TN FMAs).  Measured on B200:
+    // TN = 64 over 32 +6% on the config-5 K = 768 layers, TN = 128 over 64
+    // +7-11% on the config-4 K = 384 layers.  Tuning knob
+    // SPARSECORE_B200_XS_TN=32|64|128.
+    int tn = xs_lanes_for128(K) ? 128 : xs_lanes_for64(K) ? 64 : (xs_lanes_for(K) == 8 ? 32 : 0);
     if (const char* e = std::getenv("SPARSECORE_B200_XS_TN")) {
         const int v = std::atoi(e);
         if (v == 32 && xs_lanes_for(K) == 8) tn = 32;
         if (v == 64 && xs_lanes_for64(K)) tn = 64;
+        if (v == 128 && xs_lanes_for128(K)) tn = 128;
     }
+    if (tn == 128) return launch_xs<32>(W, X, K, N, Y, s);
     if (tn == 64) return launch_xs<16>(W, X, K, N, Y, s);
     if (tn == 32) return launch_xs<8>(W, X, K, N, Y, s);
     return -1;

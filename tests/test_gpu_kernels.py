@@ -159,10 +159,10 @@ def test_transpose_involution_and_padding_ratio():
         W.transpose(padding_ratio=-1.0)
 
 
-@pytest.mark.parametrize("path", ["rows", "xs", "xs32"])
+@pytest.mark.parametrize("path", ["rows", "xs", "xs32", "xs64"])
 def test_forward_paths_and_sddmm_variants_vs_oracle(path, monkeypatch):
-    """Both forward decompositions (row-gather and X-stationary with 64- and
-    32-column tiles), the lane and quad SDDMM kernels, ragged row lengths (one
+    """Both forward decompositions (row-gather and X-stationary with 128-,
+    64- and 32-column tiles), the lane and quad SDDMM kernels, ragged row lengths (one
     dense row among sparse ones, empty rows) and column counts around every
     dispatch threshold (partial last tiles included)."""
     import sparsecore_b200 as sl
@@ -170,8 +170,8 @@ def test_forward_paths_and_sddmm_variants_vs_oracle(path, monkeypatch):
     from sparsecore_b200 import ops
 
     monkeypatch.setenv("SPARSECORE_B200_FWD", "xs" if path.startswith("xs") else path)
-    if path == "xs32":
-        monkeypatch.setenv("SPARSECORE_B200_XS_TN", "32")
+    if path in ("xs32", "xs64"):  # default: the widest tile that fits (here 64 for W, 128 for W^T)
+        monkeypatch.setenv("SPARSECORE_B200_XS_TN", path[2:])
     d = dev()
     g = torch.Generator().manual_seed(11)
     M, K = 301, 517
