@@ -718,8 +718,10 @@ int dispatch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStrea
 // items are (column tile, block of rows), tile-major; each CTA takes a
 // contiguous run of items and reloads X only when its tile changes.
 // Numerics are identical to spmm_fwd_kernel (same per-element FMA chain).
-constexpr int kXsThreads = 512;
-constexpr int kXsWarps = kXsThreads / 32;
+// Threads per CTA: 1024 for the one-CTA-per-SM wide tiles (TN >= 64), so
+// that 32 warps hide the shared-memory latency; 512 otherwise (two CTAs).
+template <int LPR>
+__host__ __device__ constexpr int xs_threads() { return LPR >= 16 ? 1024 : 512; }
 constexpr int kXsBoxRows = 128;
 // Staged slots per row per chunk: 16, or 32 with one row per warp (TN = 128)
 // so that a chunk still fills whole warp-wide loads.
@@ -728,7 +730,7 @@ __host__ __device__ constexpr int xs_ch() { return LPR == 32 ? 32 : 16; }
 constexpr int kXsRowsPerItemMul = 4;
 
 template <int LPR>
-__global__ void __launch_bounds__(kXsThreads)
+__global__ void __launch_bounds__(xs_threads<LPR>())
 spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
                const int32_t* __restrict__ row_start, const int32_t* __restrict__ row_nnz,
                const int32_t* __restrict__ cols, const float* __restrict__ vals,
@@ -736,6 +738,7 @@ spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
                int64_t items_per_cta, unsigned* status) {
     constexpr int TN = 4 * LPR;
     constexpr int RPW = 32 / LPR;
+    constexpr int kXsWarps = xs_threads<LPR>() / 32;
     constexpr int ROWS_PER_ITEM = kXsWarps * RPW * kXsRowsPerItemMul;
     extern __shared__ __align__(128) unsigned char smem[];
     float* xs = reinterpret_cast<float*>(smem);
@@ -850,6 +853,7 @@ template <int LPR>
 int launch_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, cudaStream_t s) {
     constexpr int TN = 4 * LPR;
     constexpr int RPW = 32 / LPR;
+    constexpr int kXsWarps = xs_threads<LPR>() / 32;
     constexpr int ROWS_PER_ITEM = kXsWarps * RPW * kXsRowsPerItemMul;
     CUtensorMap map;
     if (!make_tmap_2d(&map, X, K, N, kXsBoxRows, TN)) return -1;
@@ -870,7 +874,7 @@ int launch_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, c
     if (grid > n_items) grid = n_items;
     const int64_t per_cta = (n_items + grid - 1) / grid;
     grid = (n_items + per_cta - 1) / per_cta;
-    spmm_xs_kernel<LPR><<<static_cast<unsigned>(grid), kXsThreads, smem, s>>>(
+    spmm_xs_kernel<LPR><<<static_cast<unsigned>(grid), xs_threads<LPR>(), smem, s>>>(
         map, M, N, W->row_start, W->row_nnz, W->col_indices, W->values, Y, nbox, row_chunks,
         n_items, per_cta, status);
     SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd (x-stationary)");
