@@ -83,3 +83,23 @@ def test_no_variant_means_single_graph(graphed):
     layers[0]._csr.topology_version += 1
     gs()
     assert gs.captures == 2
+
+
+def test_rigl_graph_variant_keys():
+    """RigL capture gating (host only, no layers attached): capture="update_step"
+    clones only before an update step, and the key's generation moves on
+    after every update so no cloning graph outlives its clone buffers."""
+    import sparsecore_b200 as sl
+
+    every = sl.RigL(sparsity=0.9, update_freq=3, capture="every_step")
+    upd = sl.RigL(sparsity=0.9, update_freq=3, capture="update_step")
+    seen_every, seen_upd = [], []
+    for _ in range(7):
+        seen_every.append(every.graph_variant())
+        seen_upd.append(upd.graph_variant())
+        every.step()
+        upd.step()
+    assert seen_every == [(True, 0)] * 3 + [(True, 1)] * 3 + [(True, 2)]
+    assert seen_upd == [(False, 0), (False, 0), (True, 0), (False, 0), (False, 0), (True, 1), (False, 0)]
+    with pytest.raises(ValueError):
+        sl.RigL(sparsity=0.9, capture="sometimes")
