@@ -869,7 +869,9 @@ int launch_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, c
     const int row_chunks = (M + ROWS_PER_ITEM - 1) / ROWS_PER_ITEM;
     const int64_t n_tiles = (N + TN - 1) / TN;
     const int64_t n_items = n_tiles * row_chunks;
-    const int per_sm = smem <= 112 * 1024 ? 2 : 1;
+    // Resident CTAs per SM: one for the 1024-thread wide tiles (registers),
+    // else two when the shared memory allows.
+    const int per_sm = (xs_threads<LPR>() == 1024 || smem > 112 * 1024) ? 1 : 2;
     int64_t grid = static_cast<int64_t>(num_sms()) * per_sm;
     if (grid > n_items) grid = n_items;
     const int64_t per_cta = (n_items + grid - 1) / grid;
