@@ -897,11 +897,12 @@ int fwd_path() {
 int try_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, cudaStream_t s,
            bool forced) {
     if (N < 256 || N % 4 != 0 || !aligned16(X) || !aligned16(Y) || K < 1 || K > INT_MAX) return -1;
-    // Measured on B200 (config-4/5 shapes, N = 16384): with 64-column tiles
-    // (K <= 768) the X-stationary kernel beats the row-gather kernel on every
-    // layer (384 to 3072 rows, 1-12%); with 32-column tiles only when
-    // M >= 1536 (many rows per resident tile).
-    if (!forced && W->nrows < 1536 && !xs_lanes_for64(K)) return -1;
+    // Measured on B200 (config-4/5 shapes, N = 16384): with 64- or 128-column
+    // tiles (K <= 768) the X-stationary kernel beats the row-gather kernel on
+    // every layer measured (384 to 3072 rows, 1-12%); with 32-column tiles
+    // only when M >= 1536 (many rows per resident tile).  Below 256 rows a
+    // resident tile serves too few rows; the row-gather kernel keeps those.
+    if (!forced && W->nrows < 1536 && !(xs_lanes_for64(K) && W->nrows >= 256)) return -1;
     // Tile width: the widest of 128 / 64 / 32 columns whose K x TN tile fits
     // (each staged (col, value) pair feeds TN FMAs).  Measured on B200:
     // TN = 64 over 32 +6% on the config-5 K = 768 layers, TN = 128 over 64
