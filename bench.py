@@ -36,7 +36,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-seqs", type=int, default=2, help="sequences per CPU sample step")
+    ap.add_argument("--cpu-seqs", type=int, default=None,
+                    help="sequences per CPU sample step (default: the configuration's full batch)")
     ap.add_argument("--kernel", default=None,
                     help="profiling mode: SHAPE:KIND:N runs 2 launches of one kernel "
                          "(SHAPE in %s or MxK@sparsity; KIND fwd|dw|dx|transpose|densegrad, or "
@@ -444,6 +445,10 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     router_ms = (time.perf_counter() - r0) * 1e3
 
+    # Raises if a bounded device-side wait gave up anywhere in the run (its
+    # kernel's output would have been incomplete).
+    N.check_device_status(dev)
+
     t = torch.tensor([t_ms, e2e_ms, router_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -493,13 +498,14 @@ def run_ours(args, rank, world, local_rank):
                         "library_launches_per_replay": graphed.launches_per_replay}
                        if graphed is not None else None),
         "clocks": clk,
+        "device_status": "clean: no bounded device wait timed out (checked after the run)",
         "router": {"algorithm": type(algo).__name__, "every_steps": algo.update_freq,
                    "update_plus_broadcast_ms": round(router_ms, 1),
                    "note": "no update falls inside the timed window; amortised cost per step = "
                            "update_plus_broadcast_ms / every_steps"},
     }
     if world == 1 and not args.no_cpu_baseline:
-        cb = cpu_sample(args.workload, args.cpu_seqs, 1, 2)
+        cb = cpu_sample(args.workload, args.cpu_seqs, 1, 2)  # about 25 s at config 5
         cb.pop("_config")
         cb.pop("_data")
         line["cpu_baseline"] = cb
@@ -521,12 +527,15 @@ def read_traffic(kernel):
 
 # ───────────────────────────── reference arm ─────────────────────────────
 
-def cpu_sample(workload, seqs, warmup, steps):
-    """The reference's CPU implementation of the path on a bounded sample:
-    the same model with every sparse projection on the reference's own
-    compiled kernels (OpenMP, all host threads) and stock torch CPU ops for
-    the dense parts; `seqs` sequences per step (cfg4/cfg5) or the full
-    256-sample batch (cfg2, cheap on the CPU)."""
+def cpu_sample(workload, seqs, warmup, steps, budget_s=None, min_steps=1):
+    """The reference's CPU implementation of the path: the same model with
+    every sparse projection on the reference's own compiled kernels (OpenMP,
+    all host threads) and stock torch CPU ops for the dense parts.  `seqs`
+    sequences per step (cfg4/cfg5; None = the configuration's full batch) or
+    the full 256-sample batch (cfg2).  With `budget_s`, the timed steps are
+    cut to what fits that many seconds at the warm-up step's pace (never
+    below `min_steps`).  The result states the steps, warm-up and batch that
+    actually ran; nothing is scaled or extrapolated."""
     threads = os.cpu_count() or 1
     os.environ.setdefault("OMP_NUM_THREADS", str(threads))
     torch.set_num_threads(threads)
@@ -544,34 +553,46 @@ def cpu_sample(workload, seqs, warmup, steps):
         opt.step()
         return float(loss.item())
 
+    t_step = None
     for _ in range(warmup):
+        t0 = time.perf_counter()
         step()
+        t_step = time.perf_counter() - t0
+    if budget_s is not None and t_step:
+        steps = max(min_steps, min(steps, int(budget_s / t_step)))
     t0 = time.perf_counter()
     for _ in range(steps):
         step()
     dt = time.perf_counter() - t0
+    batch = wl.batch[0].shape[0]
     return {"value": round(wl.units * steps / dt, 2), "unit": wl.unit,
-            "_config": wl.config, "_data": wl.data,
+            "_config": dict(wl.config, global_batch=batch), "_data": wl.data,
             "cores": threads if kern.kind == "reference" else 1, "kind": kern.kind,
-            "sample": f"{steps} training steps of {wl.units} {wl.unit.split('/')[0]} ({workload} "
-                      f"model, {warmup} warm-up), reference _core kernels (OpenMP) + torch CPU "
-                      f"dense ops",
+            "steps": steps, "warmup": warmup,
+            "sample": f"{steps} timed training steps (after {warmup} warm-up) of the full "
+                      f"{workload} batch: {batch} x {wl.units // batch} = {wl.units} "
+                      f"{wl.unit.split('/')[0]} per step; reference _core kernels (OpenMP, "
+                      f"{threads} threads) + torch CPU dense ops; nothing extrapolated",
             "ms_per_step": round(dt / steps * 1e3, 1)}
+
+
+# Timed seconds the reference arm may spend (a config-5 step takes about
+# 8.5 s on 16 host cores, so the default 20 steps fit).
+REFERENCE_BUDGET_S = 200.0
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return None
-    cb = cpu_sample(args.workload, args.cpu_seqs, max(1, min(args.warmup, 2)),
-                    max(1, min(args.steps, 5)))
+    cb = cpu_sample(args.workload, args.cpu_seqs, max(1, min(args.warmup, 1)), args.steps,
+                    budget_s=REFERENCE_BUDGET_S, min_steps=3)
     ref = {"config": cb.pop("_config"), "data": cb.pop("_data")}
     return {
         "metric": METRIC, "impl": "reference", "value": cb["value"], "unit": cb["unit"],
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "n_gpus": world, "steps": cb["steps"], "warmup": cb["warmup"],
         "ms_per_step": cb["ms_per_step"], "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": ref["data"],
-        "config": dict(ref["config"], global_batch=ref["config"]["global_batch"] * world,
-                       parallelism=f"dp{world}"),
+        "config": dict(ref["config"], parallelism="dp1 (rank 0 on the host cores)"),
         "cpu_baseline": cb,
         "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},

@@ -111,8 +111,8 @@ SL_API int sl_transpose_fill(const sl_csr* W, const sl_csr* WT, int64_t* perm,
  * call cudaMalloc -- e.g. code running inside a memory pool or allocator
  * hook, a real-time loop that forbids allocation, or an embedding host that
  * owns all device memory -- and so cannot provide the scratch buffer that
- * sl_transpose_count / sl_transpose_fill need.  Same result as those two
- * calls (sparselab/layout.py:460 transpose_with_perm), in one call:
+ * sl_transpose_count / sl_transpose_fill need.  It writes the same WT and
+ * perm as sl_transpose_count followed by sl_transpose_fill, in one call:
  *   * scratch is a file-scope device array of 4 MiB (2^20 int32 counters)
  *     that every GPU loading the library holds until the process exits;
  *     inputs need ceil(nrows/32) * ncols <= 2^20 (and ncols <= 57344), else
@@ -124,13 +124,19 @@ SL_API int sl_transpose_fill(const sl_csr* W, const sl_csr* WT, int64_t* perm,
  *     SL_ERR_INVALID.  The true total capacity is written to *out_total_dev;
  *     entries past it are padding (-1, 0.0f, perm -1);
  *   * the first call on a device looks up the array's device address
- *     (cudaGetSymbolAddress) with that device current; make that first call
- *     before any stream capture;
+ *     (cudaGetSymbolAddress) with that device current.  If no other kernel
+ *     of this library has run on that device yet, that lookup is also what
+ *     makes CUDA load the library's device code there (with lazy module
+ *     loading, the CUDA 12 default) and place the array: memory the driver
+ *     sets aside once.  Make that first call at initialisation, before any
+ *     stream capture and before the point from which nothing may allocate;
  *   * every call shares the one array and leaves its contents behind (the
  *     kernels overwrite all of it they read, so nothing must be cleared);
  *     calls whose work overlaps on the GPU (different streams, or several
  *     host threads) race on it and give wrong results -- serialise them.
- * Allocates no device or host memory and calls no allocating routine. */
+ * After that first call a successful call allocates no device or host
+ * memory and calls no allocating routine; a failing call formats its
+ * message for sl_last_error() in a host string. */
 SL_API int sl_transpose_with_perm_noalloc(const sl_csr* W, double one_plus_padding_ratio,
                                    const sl_csr* WT, int64_t* perm,
                                    int64_t* out_total_dev, void* stream);

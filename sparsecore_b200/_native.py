@@ -165,3 +165,32 @@ def check(rc: int, fn: str = "") -> None:
     if rc == SL_ERR_INVALID:
         raise ValueError(msg)
     raise RuntimeError(msg)
+
+
+STATUS_TIMEOUT_BIT = 1
+
+
+def check_device_status(device: torch.device | int | None = None, sync: bool = True) -> None:
+    """Read and clear the library's device status word; raise if a bounded
+    device-side wait gave up since the last check.
+
+    The TMA-fed kernels (X-stationary forward, tiled SDDMM) bound every
+    mbarrier wait.  A wait that runs out raises bit 0 of a per-device status
+    word and the kernel returns early, so its output (Y or dW) is incomplete;
+    the C call itself has already returned SL_OK by then.  This check turns
+    that bit into ``RuntimeError`` (the C-ABI's SL_ERR_TIMEOUT).  It costs a
+    device synchronisation (``sync=True``) plus a 4-byte read, so callers run
+    it where they synchronise anyway: router updates, graph re-captures, the
+    end of a benchmark."""
+    dev = require_cuda(None if device is None else torch.device("cuda", device)
+                       if isinstance(device, int) else device)
+    if sync:
+        torch.cuda.synchronize(dev)
+    st = ctypes.c_uint(0)
+    with torch.cuda.device(dev):
+        check(lib().sl_device_status(1, ctypes.byref(st)), "sl_device_status")
+    if st.value & STATUS_TIMEOUT_BIT:
+        raise RuntimeError(
+            f"sparsecore_b200: a bounded device-side wait timed out on {dev} (status word "
+            f"0x{st.value:x}, SL_ERR_TIMEOUT): the outputs of kernels launched since the last "
+            "status check are incomplete")

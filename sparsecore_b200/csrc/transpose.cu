@@ -20,7 +20,6 @@
 //                contention; a barrier between rows keeps source-row order.
 #include <cmath>
 #include <mutex>
-#include <vector>
 
 #include "common.cuh"
 
@@ -235,21 +234,26 @@ namespace {
 constexpr int64_t kNoAllocScratchInts = int64_t(1) << 20;  // 4 MiB per device
 __device__ __align__(256) int32_t g_noalloc_scratch[kNoAllocScratchInts];
 
+// Device addresses of the array, one slot per device ordinal, in a fixed
+// table: the lookup itself allocates nothing on the host either.
+constexpr int kNoAllocMaxDevices = 64;
+int32_t* g_noalloc_addr[kNoAllocMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
 int noalloc_scratch(int32_t** out) {
-    static std::mutex mu;
-    static std::vector<int32_t*> addr;
     int dev = 0;
     if (int rc = cuda_status(cudaGetDevice(&dev), "sl_transpose_with_perm_noalloc")) return rc;
-    std::lock_guard<std::mutex> lock(mu);
-    if (dev >= static_cast<int>(addr.size())) addr.resize(dev + 1, nullptr);
-    if (addr[dev] == nullptr) {
+    if (dev < 0 || dev >= kNoAllocMaxDevices)
+        return fail(SL_ERR_UNSUPPORTED, "sl_transpose_with_perm_noalloc: device ordinal above 63");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_addr[dev] == nullptr) {
         void* p = nullptr;
         if (int rc = cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scratch),
                                  "sl_transpose_with_perm_noalloc: cudaGetSymbolAddress"))
             return rc;
-        addr[dev] = static_cast<int32_t*>(p);
+        g_noalloc_addr[dev] = static_cast<int32_t*>(p);
     }
-    *out = addr[dev];
+    *out = g_noalloc_addr[dev];
     return SL_OK;
 }
 

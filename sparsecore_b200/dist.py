@@ -30,6 +30,7 @@ import torch
 import torch.distributed as dist
 
 from . import _native as N
+from . import ops
 
 
 @dataclass
@@ -168,6 +169,10 @@ class SparseDataParallel:
             fo += cap
             csr._sync_row_nnz_from_device()
             csr.topology_version_ = int(v)
+            # The cached W^T is keyed by topology_version only; a rank whose
+            # own mask differed at the same version would otherwise keep
+            # using a W^T (and perm) of its old mask for dX.
+            ops._transpose_cache.pop(id(csr), None)
 
     def topology_checksum(self) -> list[int]:
         """All ranks' mask checksums (equal when the replicas agree)."""

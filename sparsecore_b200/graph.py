@@ -66,7 +66,7 @@ class GraphedStep:
             self.graph = None
         for m in self.layers:
             ops._cached_transpose(m._csr)  # rebuild (eagerly) before recording
-        torch.cuda.synchronize()
+        self.check_status()
         v = self._variant()
         self._graphs.pop(v, None)
         g = torch.cuda.CUDAGraph()
@@ -78,6 +78,15 @@ class GraphedStep:
         self._graphs[v] = (g, loss, launches)
         self._key = self._topology()
         self.captures += 1
+
+    def check_status(self) -> None:
+        """Synchronise and raise RuntimeError if a bounded device-side wait
+        gave up since the last check (the replays since then produced
+        incomplete gradients).  Runs at every (re-)capture; call it at any
+        other point that synchronises, e.g. where the loss is read."""
+        devs = {m._csr.values.device for m in self.layers} or {torch.device("cuda", torch.cuda.current_device())}
+        for dev in devs:
+            N.check_device_status(dev)
 
     def __call__(self) -> torch.Tensor:
         v = self._variant()

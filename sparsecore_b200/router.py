@@ -105,6 +105,11 @@ class DynamicSparsityAlgorithm(SparsityAlgorithm):
     def step(self) -> None:
         self._step_idx += 1
         if self._step_idx % self.update_freq == 0:
+            # The update reads values and gradients the kernels produced, and
+            # synchronises anyway: first make sure no bounded device wait
+            # gave up since the last check (its outputs would be incomplete).
+            for dev in {m._csr.values.device for m in self.layers}:
+                N.check_device_status(dev)
             self.update()
             self.last_update_step = self._step_idx
 

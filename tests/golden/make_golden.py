@@ -224,8 +224,11 @@ def gen_mlp_trajectory(sl, meta: dict, steps: int = 250) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("SPARSELAB_REF"),
+                    help="root of the reference source tree (or set SPARSELAB_REF)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("the reference source tree is required: --ref DIR or SPARSELAB_REF=DIR")
     sl, core = load_reference(args.ref)
     meta = {"numpy": np.__version__, "torch": torch.__version__, "reference": "sparselab 0.2.x"}
     arrays: dict = {}

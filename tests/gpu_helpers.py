@@ -50,3 +50,31 @@ def oracle_csr(W):
 
     return O.CSR(W.nrows, W.ncols, host(W.values).copy(), host(W.col_indices).copy(),
                  host(W.row_start).copy(), host(W.row_nnz).copy(), host(W.row_capacity).copy())
+
+
+def launched_kernels(fn):
+    """Run ``fn`` under the CUDA activity profiler and return (its result,
+    the names of the GPU kernels it launched), so a parity test can assert
+    which kernel actually produced the values it checks."""
+    from torch.autograd import DeviceType
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        out = fn()
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if e.device_type == DeviceType.CUDA]
+    return out, names
+
+
+def random_csr(M, K, density, seed, block=None, device=None):
+    """PaddedCSR from a seeded uniform mask (values N(0,1)); ``block`` =
+    (rows, cols) of a fully dense top-left block."""
+    import sparsecore_b200 as sl
+
+    g = torch.Generator().manual_seed(seed)
+    mask = torch.rand(M, K, generator=g) < density
+    if block is not None:
+        mask[:block[0], :block[1]] = True
+    Wd = torch.randn(M, K, generator=g) * mask
+    return sl.PaddedCSR.from_dense(Wd.to(device or dev()))

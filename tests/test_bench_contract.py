@@ -29,13 +29,15 @@ def test_reference_arm_prints_the_contract_line():
                 "cpu_baseline"):
         assert key in line, key
     assert line["impl"] == "reference"
-    assert line["value"] > 0 and line["n_gpus"] == 1 and line["steps"] == 1
+    # at least 3 timed steps after 1 warm-up, printed as they ran
+    assert line["value"] > 0 and line["n_gpus"] == 1 and line["steps"] == 3
+    assert line["warmup"] == 1 and line["config"]["global_batch"] == 256
     assert "workload" in line["config"]
     assert line["e2e"] == {"value": line["value"], "unit": line["unit"], "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
     cb = line["cpu_baseline"]
     assert cb["kind"] in ("reference", "port") and cb["cores"] >= 1 and cb["sample"]
-    assert cb["value"] == line["value"]
+    assert cb["value"] == line["value"] and cb["steps"] == line["steps"]
 
 
 @pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-GPU behaviour")

@@ -140,6 +140,13 @@ def _worker_broadcast(rank, world, port, q):
                 L._csr.col_indices.add_(1)
                 L._csr.values.mul_(3.0)
                 L._csr.row_nnz[0] = 0
+        from sparsecore_b200 import ops
+
+        # Both ranks cached a transpose at the same topology version, built
+        # from different masks on rank 1: the broadcast must drop it.
+        for L in layers:
+            ops._transpose_cache[id(L._csr)] = (L._csr.topology_version, (L._csr.nrows, L._csr.ncols),
+                                                "stale W^T", "stale perm")
         before = ddp.topology_checksum()
         ddp.broadcast_topology(src=0)
         after = ddp.topology_checksum()
@@ -150,6 +157,7 @@ def _worker_broadcast(rank, world, port, q):
             ok &= torch.equal(L._csr.values, R.values)
             ok &= torch.equal(L._csr.row_nnz, R.row_nnz)
             ok &= L._values.data_ptr() == L._csr.values.data_ptr()  # alias kept
+            ok &= id(L._csr) not in ops._transpose_cache  # no stale W^T survives
         q.put((rank, bool(ok)))
     except Exception as e:  # pragma: no cover
         q.put((rank, repr(e)))

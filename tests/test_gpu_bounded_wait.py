@@ -25,3 +25,16 @@ def test_bounded_wait_times_out_and_reports():
     a = torch.arange(10.0, device="cuda")
     assert float(a.sum().item()) == 45.0
     assert lib.sl_selftest_bounded_wait(0, None) == N.SL_ERR_INVALID
+
+
+def test_python_layer_raises_on_timeout():
+    """The status check that routers, graph re-captures and the benchmark run
+    turns a timed-out wait into RuntimeError, once, and clears the word."""
+    from sparsecore_b200 import _native as N
+
+    dev = torch.device("cuda", 0)
+    N.check_device_status(dev)  # start clean
+    N.check(N.lib().sl_selftest_bounded_wait(1 << 12, N.stream_ptr(dev)))
+    with pytest.raises(RuntimeError, match="timed out"):
+        N.check_device_status(dev)
+    N.check_device_status(dev)  # cleared by the read

@@ -195,10 +195,12 @@ def test_forward_paths_and_sddmm_variants_vs_oracle(path, monkeypatch):
 @pytest.mark.parametrize("M,K,N,block", [(301, 517, 256, False), (700, 300, 512, True),
                                          (96, 2000, 288, False), (1000, 1000, 320, True),
                                          (2100, 3100, 256, True)])
-def test_tiled_sddmm_matches_slot_kernels_and_oracle(M, K, N, block, monkeypatch):
-    """The tiled SDDMM (large N) against the per-slot kernels and the oracle:
-    edge tiles (M, K not multiples of the tile), and a dense block that puts
-    thousands of slots into one tile (several batches per tile)."""
+def test_mid_n_sddmm_and_forward_vs_oracle(M, K, N, block, monkeypatch):
+    """N = 256-512, below the tiled SDDMM's N >= 1024 threshold: the quad
+    SDDMM kernel (the tile-order knob has no effect here, so all three
+    launches below run it) and the forward / dX kernels against the oracle,
+    with edge rows and a dense block.  The tiled kernel's own parity cases
+    are in test_gpu_sddmm_tiled.py."""
     import sparsecore_b200 as sl
     from oracle import oracle as O
     from sparsecore_b200 import ops
@@ -213,20 +215,20 @@ def test_tiled_sddmm_matches_slot_kernels_and_oracle(M, K, N, block, monkeypatch
     X = torch.randn(K, N, generator=g)
     dY = torch.randn(M, N, generator=g)
     Wo = oracle_csr(W)
-    # forward on the same shapes: K > 1536 takes the K-blocked X-stationary kernel
+    # forward on the same shapes (K > 1536 runs the row-gather kernel)
     assert bits_equal(sl.spmm(W, X.to(d)), O.spmm(Wo, X.numpy()))
     WT, _ = sl.transpose_with_perm(W)
     WTo, _ = O.transpose_with_perm(Wo)
     assert bits_equal(ops._spmm_raw(WT, dY.to(d)), O.spmm(WTo, dY.numpy()))
-    tiled = ops._sddmm_raw(W, dY.to(d), X.to(d))  # paired-slot lane mapping
+    dw = ops._sddmm_raw(W, dY.to(d), X.to(d))
     other = "row" if K > M else "col"  # the tile order the default did not take
     monkeypatch.setenv("SPARSECORE_B200_DW_ORDER", other)
-    tiled_other = ops._sddmm_raw(W, dY.to(d), X.to(d))
+    dw_other_order = ops._sddmm_raw(W, dY.to(d), X.to(d))
     monkeypatch.setenv("SPARSECORE_B200_DW", "quad")
     per_slot = ops._sddmm_raw(W, dY.to(d), X.to(d))
-    assert bits_equal(tiled, per_slot)
-    assert bits_equal(tiled_other, per_slot)
-    assert bits_equal(tiled, O.sddmm(Wo, dY.numpy(), X.numpy()))
+    assert bits_equal(dw, per_slot)
+    assert bits_equal(dw_other_order, per_slot)
+    assert bits_equal(dw, O.sddmm(Wo, dY.numpy(), X.numpy()))
 
 
 @pytest.mark.parametrize("M,K,s,pr", [(70, 50, 0.5, 0.2), (9, 13, 0.0, 0.0), (129, 20000, 0.995, 0.2),

@@ -34,13 +34,16 @@ def graphed(monkeypatch):
     monkeypatch.setattr(torch.cuda, "graph", _FakeCtx)
     monkeypatch.setattr(torch.cuda, "synchronize", lambda *a, **k: None)
     monkeypatch.setattr(ops, "_cached_transpose", lambda csr: None)
+    status_checks = []
+    monkeypatch.setattr(graph.N, "check_device_status", lambda dev: status_checks.append(dev))
     layers = []
     for _ in range(2):
         m = SparseLinear.__new__(SparseLinear)
         torch.nn.Module.__init__(m)
-        m._csr = types.SimpleNamespace(topology_version=0)
+        m._csr = types.SimpleNamespace(topology_version=0, values=torch.zeros(1))
         layers.append(m)
     model = torch.nn.Sequential(*layers)
+    monkeypatch.setattr(graph, "status_checks", status_checks, raising=False)
     return graph, model, layers
 
 
@@ -58,6 +61,7 @@ def test_one_graph_per_variant_and_recapture_on_topology_change(graphed):
     for _ in range(3):
         gs()
     assert gs.captures == 1 and _FakeGraph.replays == 3
+    assert len(graph.status_checks) == 1  # the device status is read at each capture
     state["variant"] = (True, 0)   # e.g. RigL about to clone X / dY
     gs()
     gs()

@@ -93,3 +93,67 @@ def test_noalloc_transpose_rejects_oversize_and_short_buffers():
                                             N.P(1), W._stream())
     assert rc == N.SL_ERR_INVALID
     assert b"required" in lib.sl_last_error()
+
+
+_FIRST_CALL_SCRIPT = r"""
+import ctypes, math, sys
+import numpy as np
+import torch
+sys.path.insert(0, sys.argv[1])
+from sparsecore_b200 import _native as N
+
+# A padded CSR built with numpy and plain copies: no library kernel runs
+# before the allocation-free entry point.
+rng = np.random.default_rng(5)
+M, K, opp = 200, 333, 1.2
+mask = rng.random((M, K)) >= 0.85
+nnz = mask.sum(1).astype(np.int32)
+cap = np.maximum(1, np.ceil(nnz * opp)).astype(np.int32)
+rs = np.concatenate([[0], np.cumsum(cap)[:-1]]).astype(np.int32)
+tot = int(cap.sum())
+vals = np.zeros(tot, np.float32); cols = np.full(tot, -1, np.int32)
+for i in range(M):
+    c = np.nonzero(mask[i])[0]
+    cols[rs[i]:rs[i] + len(c)] = c
+    vals[rs[i]:rs[i] + len(c)] = rng.standard_normal(len(c)).astype(np.float32)
+d = torch.device("cuda", 0)
+t = {k: torch.from_numpy(v).to(d) for k, v in
+     dict(vals=vals, cols=cols, rs=rs, nnz=nnz, cap=cap).items()}
+W = N.SlCsr(M, K, tot, t["vals"].data_ptr(), t["cols"].data_ptr(), t["rs"].data_ptr(),
+            t["nnz"].data_ptr(), t["cap"].data_ptr())
+bound = int(math.floor(opp * tot)) + K + 2
+rows = torch.empty(3, K, dtype=torch.int32, device=d)
+wv = torch.empty(bound, dtype=torch.float32, device=d)
+wc = torch.empty(bound, dtype=torch.int32, device=d)
+perm = torch.empty(bound, dtype=torch.int64, device=d)
+total = torch.zeros(1, dtype=torch.int64, device=d)
+WT = N.SlCsr(K, M, bound, wv.data_ptr(), wc.data_ptr(), rows[2].data_ptr(), rows[0].data_ptr(),
+             rows[1].data_ptr())
+N.check(N.lib().sl_transpose_with_perm_noalloc(ctypes.byref(W), opp, ctypes.byref(WT),
+                                               N.ptr(perm), N.ptr(total), None))
+torch.cuda.synchronize()
+n = int(total.item())
+
+import sparsecore_b200 as sl
+P = sl.PaddedCSR(M, K, vals, cols, rs, nnz, cap, device=d)
+RT, rperm = sl.transpose_with_perm(P, padding_ratio=opp - 1.0)
+ok = (n == RT.total_capacity and torch.equal(rows[0], RT.row_nnz)
+      and torch.equal(rows[1], RT.row_capacity) and torch.equal(rows[2], RT.row_start)
+      and torch.equal(wc[:n], RT.col_indices) and torch.equal(perm[:n], rperm)
+      and torch.equal(wv[:n].view(torch.int32), RT.values.view(torch.int32)))
+print("FIRST_CALL_OK" if ok else "FIRST_CALL_MISMATCH")
+"""
+
+
+def test_noalloc_transpose_as_first_library_call_in_a_fresh_process():
+    """The first call on a device also looks up the scratch array's address
+    (and, with lazy module loading, makes CUDA load the library's device
+    code): run it before any other kernel of the library in a new process."""
+    import os
+    import subprocess
+    import sys
+
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = subprocess.run([sys.executable, "-c", _FIRST_CALL_SCRIPT, repo], capture_output=True,
+                         text=True, timeout=600)
+    assert "FIRST_CALL_OK" in out.stdout, out.stdout + out.stderr
