@@ -53,6 +53,13 @@ def parse():
                          "critical-path kernels get SMs first) or torch's default stream")
     ap.add_argument("--sweep", action="store_true",
                     help="config-3 standalone SpMM sweep: one JSON line per cell")
+    ap.add_argument("--flush", choices=["read", "write"], default="read",
+                    help="sweep / kernel timing: L2 flush by reading (default) or writing a "
+                         "256 MB buffer between launches")
+    ap.add_argument("--sweep-n", default="1,32,256,2048,8192",
+                    help="comma-separated N values of the sweep")
+    ap.add_argument("--sweep-sparsity", default="0.5,0.8,0.9,0.95,0.99",
+                    help="comma-separated sparsities of the sweep")
     return ap.parse_args()
 
 
@@ -114,19 +121,32 @@ def run_kernel_case(spec):
     print(json.dumps({"kernel_case": spec, "M": M, "K": K, "N": N, "nnz": W.nnz}))
 
 
+FLUSH_MODE = {"mode": "read"}
+
+
 def graph_time_ms(fn, flush_buf, reps=10):
     """Device time of one launch of `fn`: CUDA-graph replay of reps x
     [L2 flush, fn] minus reps x [L2 flush], so neither host launch overhead
-    nor a warm L2 enters the number (flush_buf must exceed the L2)."""
+    nor a warm L2 enters the number (flush_buf must exceed the L2).  The
+    flush reads the buffer (mode "read", the default): that evicts the
+    kernel's inputs without leaving dirty lines in L2, whose write-back would
+    otherwise be charged to the timed kernel.  Mode "write" overwrites it."""
     for _ in range(3):
         fn()
     torch.cuda.synchronize()
+    sink = torch.empty((), dtype=flush_buf.dtype, device=flush_buf.device)
+
+    def flush():
+        if FLUSH_MODE["mode"] == "write":
+            flush_buf.zero_()
+        else:
+            torch.sum(flush_buf, dim=0, out=sink)
 
     def capture(with_fn):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             for _ in range(reps):
-                flush_buf.zero_()
+                flush()
                 if with_fn:
                     fn()
         return g
@@ -156,17 +176,17 @@ def run_sweep(args):
     hbm, src, sm_max = peaks()
     fp32 = 148 * 128 * 2 * sm_max * 1e6 / 1e12
 
-    flush_buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MB > L2
+    flush_buf = torch.zeros(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MB > L2
 
     def t_ms(fn):
         return graph_time_ms(fn, flush_buf)
 
     for (M, K) in [(4096, 4096), (16384, 4096)]:
-        for s in (0.5, 0.8, 0.9, 0.95, 0.99):
+        for s in [float(v) for v in args.sweep_sparsity.split(",")]:
             W = _sweep_matrix(M, K, s)
             WT, _ = sl.transpose_with_perm(W)
             nnz = W.nnz
-            for N in (1, 32, 256, 2048, 8192):
+            for N in [int(v) for v in args.sweep_n.split(",")]:
                 if 4 * (K * N + M * N) * 3 > 60e9:
                     continue
                 X = torch.randn(K, N, device="cuda")
@@ -610,6 +630,7 @@ def main():
         run_kernel_case(args.kernel)
         return
     if args.sweep:
+        FLUSH_MODE["mode"] = args.flush
         run_sweep(args)
         return
     if args.impl == "reference":

@@ -24,8 +24,8 @@ NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-lineinfo", "-O3", "-std=c++17",
     "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
-    "-shared", "-cudart", "shared",
 ]
+LINK_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-cudart", "shared"]
 
 
 def nvcc() -> str:
@@ -49,18 +49,42 @@ def _stale() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
+    """Compile every csrc/*.cu to an object (in parallel), then link the
+    shared library."""
     if not force and not _stale():
         return LIB_PATH
+    from concurrent.futures import ThreadPoolExecutor
+
     os.makedirs(LIB_DIR, exist_ok=True)
+    obj_dir = os.path.join(LIB_DIR, "obj")
+    os.makedirs(obj_dir, exist_ok=True)
+    cc = nvcc()
+
+    def compile_one(src):
+        obj = os.path.join(obj_dir, os.path.basename(src) + ".o")
+        cmd = [cc, *NVCC_FLAGS, "-Xptxas", "-v", "-c", src, "-o", obj]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        return obj, cmd, res
+
+    with ThreadPoolExecutor(max_workers=max(1, min(len(sources()), os.cpu_count() or 1))) as ex:
+        results = list(ex.map(compile_one, sources()))
+    log = []
+    failed = False
+    for _, cmd, res in results:
+        log.append(" ".join(cmd) + "\n" + res.stdout + res.stderr)
+        failed |= res.returncode != 0
     tmp = LIB_PATH + ".tmp"
-    cmd = [nvcc(), *NVCC_FLAGS, "-Xptxas", "-v", *sources(), "-o", tmp]
-    if verbose:
-        print(" ".join(cmd))
-    res = subprocess.run(cmd, capture_output=True, text=True)
+    if not failed:
+        cmd = [cc, *LINK_FLAGS, *[o for o, _, _ in results], "-o", tmp]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        log.append(" ".join(cmd) + "\n" + res.stdout + res.stderr)
+        failed = res.returncode != 0
     with open(os.path.join(LIB_DIR, "build.log"), "w") as f:
-        f.write(" ".join(cmd) + "\n" + res.stdout + res.stderr)
-    if res.returncode != 0:
-        sys.stderr.write(res.stdout + res.stderr)
+        f.write("\n".join(log))
+    if verbose:
+        print("\n".join(log))
+    if failed:
+        sys.stderr.write("\n".join(log))
         raise RuntimeError("nvcc failed building sparsecore_b200 (see _lib/build.log)")
     os.replace(tmp, LIB_PATH)
     return LIB_PATH

@@ -946,7 +946,10 @@ extern "C" int sl_spmm_fwd(const sl_csr* W, const float* X, int64_t K, int64_t N
         if (rc >= 0) return rc;
     }
     if (N == 1 && spmv_lane_enabled(W)) {
-        const int rc = launch_spmv(W, X, K, Y, s);
+        // SPARSECORE_B200_N1=lane keeps the cp.async lane kernel (tests).
+        const char* e = std::getenv("SPARSECORE_B200_N1");
+        int rc = (e != nullptr && e[0] == 'l') ? -1 : launch_spmv_bulk(W, X, K, Y, s);
+        if (rc < 0) rc = launch_spmv(W, X, K, Y, s);
         if (rc >= 0) return rc;
     }
     if (N == 4 || N == 8) {

@@ -233,14 +233,16 @@ def test_mid_n_sddmm_and_forward_vs_oracle(M, K, N, block, monkeypatch):
 
 @pytest.mark.parametrize("M,K,s,pr", [(70, 50, 0.5, 0.2), (9, 13, 0.0, 0.0), (129, 20000, 0.995, 0.2),
                                       (300, 3000, 0.9, 0.0), (1000, 700, 0.97, 0.2),
-                                      (12000, 300, 0.9, 0.0)])
+                                      (12000, 300, 0.9, 0.0), (7, 5, 0.3, 0.0), (4733, 1001, 0.8, 0.0),
+                                      (300, 17000, 0.9, 0.2)])
 def test_spmv_lane_kernel_matches_oracle_and_warp_kernel(M, K, s, pr, monkeypatch):
-    """N = 1: forward / dX on the lane-per-row kernel (cp.async row
-    segments) and the streaming SDDMM, against the oracle and the general
-    kernels: ragged and empty rows, rows whose 4-slot groups start unaligned
-    or run past the arrays' end (no padding), K above the shared-memory X
-    limit, one long row among short ones, and more rows than two warps per
-    SM (the second lane-kernel configuration)."""
+    """N = 1: forward / dX on the lane-per-row kernels (bulk-copied row
+    windows by default, both window sizes; the cp.async variant) and the
+    streaming SDDMM, against the oracle and the general kernels: ragged and
+    empty rows, rows whose 4-slot groups start unaligned or run past the
+    arrays' end (no padding, total capacity not a multiple of 4), K above
+    the shared-memory X limit, one long row among short ones, and more rows
+    than one or two warps per SM (the other configurations)."""
     import sparsecore_b200 as sl
     from oracle import oracle as O
     from sparsecore_b200 import ops
@@ -263,6 +265,14 @@ def test_spmv_lane_kernel_matches_oracle_and_warp_kernel(M, K, s, pr, monkeypatc
     assert bits_equal(y, O.spmm(Wo, X.numpy()))
     assert bits_equal(dx, O.spmm(WTo, dY.numpy()))
     assert bits_equal(dw, O.sddmm(Wo, dY.numpy(), X.numpy()))
+    for win in ("64", "128"):  # both bulk-window configurations
+        monkeypatch.setenv("SPARSECORE_B200_N1_WIN", win)
+        assert bits_equal(sl.spmm(W, X.to(d)), y), win
+        assert bits_equal(ops._spmm_raw(WT, dY.to(d)), dx), win
+    monkeypatch.delenv("SPARSECORE_B200_N1_WIN")
+    monkeypatch.setenv("SPARSECORE_B200_N1", "lane")  # the cp.async lane kernel
+    assert bits_equal(sl.spmm(W, X.to(d)), y)
+    assert bits_equal(ops._spmm_raw(WT, dY.to(d)), dx)
     monkeypatch.setenv("SPARSECORE_B200_N1", "warp")
     assert bits_equal(sl.spmm(W, X.to(d)), y)
     assert bits_equal(ops._spmm_raw(WT, dY.to(d)), dx)
