@@ -53,11 +53,16 @@ def parse():
                          "critical-path kernels get SMs first) or torch's default stream")
     ap.add_argument("--sweep", action="store_true",
                     help="config-3 standalone SpMM sweep: one JSON line per cell")
-    ap.add_argument("--flush", choices=["read", "write"], default="read",
+    ap.add_argument("--flush", choices=["read", "write"], default="write",
                     help="sweep / kernel timing: L2 flush by reading (default) or writing a "
                          "256 MB buffer between launches")
     ap.add_argument("--sweep-n", default="1,32,256,2048,8192",
                     help="comma-separated N values of the sweep")
+    ap.add_argument("--sweep-shapes", default="4096x4096,16384x4096",
+                    help="comma-separated MxK shapes of the sweep (config 1 is 256x784)")
+    ap.add_argument("--sweep-cpu-max-n", type=int, default=256,
+                    help="time the reference's CPU kernels beside the GPU on cells with N up to "
+                         "this (0 = never)")
     ap.add_argument("--sweep-sparsity", default="0.5,0.8,0.9,0.95,0.99",
                     help="comma-separated sparsities of the sweep")
     return ap.parse_args()
@@ -121,16 +126,16 @@ def run_kernel_case(spec):
     print(json.dumps({"kernel_case": spec, "M": M, "K": K, "N": N, "nnz": W.nnz}))
 
 
-FLUSH_MODE = {"mode": "read"}
+FLUSH_MODE = {"mode": "write"}
 
 
 def graph_time_ms(fn, flush_buf, reps=10):
     """Device time of one launch of `fn`: CUDA-graph replay of reps x
     [L2 flush, fn] minus reps x [L2 flush], so neither host launch overhead
     nor a warm L2 enters the number (flush_buf must exceed the L2).  The
-    flush reads the buffer (mode "read", the default): that evicts the
-    kernel's inputs without leaving dirty lines in L2, whose write-back would
-    otherwise be charged to the timed kernel.  Mode "write" overwrites it."""
+    flush overwrites the buffer (mode "write", the default) or reads it
+    (mode "read": evicts without leaving dirty lines in L2; measured no
+    faster on B200)."""
     for _ in range(3):
         fn()
     torch.cuda.synchronize()
@@ -181,7 +186,14 @@ def run_sweep(args):
     def t_ms(fn):
         return graph_time_ms(fn, flush_buf)
 
-    for (M, K) in [(4096, 4096), (16384, 4096)]:
+    shapes = [tuple(int(v) for v in sh.split("x")) for sh in args.sweep_shapes.split(",")]
+    if args.sweep_cpu_max_n > 0:
+        threads = os.cpu_count() or 1
+        os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+        print(json.dumps({"cpu": {"threads": threads, "model": cpu_model(),
+                                  "method": "reference _core kernels, median of 30 trials "
+                                            "(3 above 1 s) after warm-up"}}), flush=True)
+    for (M, K) in shapes:
         for s in [float(v) for v in args.sweep_sparsity.split(",")]:
             W = _sweep_matrix(M, K, s)
             WT, _ = sl.transpose_with_perm(W)
@@ -206,10 +218,31 @@ def run_sweep(args):
                                   "fp32_frac": round(tfl / fp32, 3),
                                   "bound": "hbm" if hbm_floor >= fma_floor else "fp32-fma",
                                   "binding_frac": round(max(hbm_floor, fma_floor) / ms, 3)}
+                if 0 < N <= args.sweep_cpu_max_n:
+                    from oracle import oracle as O
+                    from oracle import ref_arm
+
+                    h = lambda t: t.detach().cpu().numpy().copy()  # noqa: E731
+                    p = O.CSR(M, K, h(W.values), h(W.col_indices), h(W.row_start), h(W.row_nnz),
+                              h(W.row_capacity))
+                    ct = ref_arm.kernel_times(p, X.cpu().numpy(), dY.cpu().numpy())
+                    cell["cpu_ms"] = ct
+                    cell["speedup_vs_cpu"] = {k: round(ct[k] / cell[k]["ms"], 1)
+                                              for k in ("fwd", "dw", "dx")}
                 print(json.dumps(cell), flush=True)
                 del X, dY
             del W, WT
             torch.cuda.empty_cache()
+
+
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def peaks():

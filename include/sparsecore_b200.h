@@ -54,6 +54,10 @@ typedef struct sl_csr {
 
 /* Message of the last failed call on this host thread ("" if none). */
 SL_API const char* sl_last_error(void);
+/* Name of the kernel that the last sl_spmm_fwd / sl_sddmm_dw call on this
+ * host thread launched (a diagnostic with no reference counterpart: tests
+ * use it to prove which decomposition produced the values they check). */
+SL_API const char* sl_last_kernel(void);
 /* Library version string. */
 SL_API const char* sl_version(void);
 /* Status word of the current device (synchronous): bit 0 set = a bounded

@@ -153,3 +153,43 @@ def linear_factory(kern):
     def make(fin, fout, sparsity, bias=False):
         return RefSparseLinear(fin, fout, sparsity, kern, bias=bias)
     return make
+
+
+def kernel_times(p: O.CSR, X: np.ndarray, dY: np.ndarray) -> dict:
+    """Host-core time of the reference's own kernels on one sweep cell, by
+    the reference's timing method (examples/profile_phase1_timing_table.py
+    :45-59): warm-up calls, then the median of 30 trials, cut to the median
+    of 3 for calls over 1 s (and to one warm-up for calls over 0.2 s).
+    Forward ``spmm_simd(W, X)``, SDDMM ``spmm_grad_w_simd(W, dY, X)`` and dX
+    ``spmm_simd(W^T, dY)`` run the compiled reference ``_core`` (kind
+    "reference"); the transpose is the reference's Python algorithm
+    (sparselab/layout.py:460), restated in numpy here (kind "port").
+    Milliseconds per call."""
+    import statistics
+    import time
+
+    kern = kernels()
+    W = kern.make(p)
+    pT, _ = O.transpose_with_perm(p)
+    WT = kern.make(pT)
+
+    def timeit(fn):
+        t0 = time.perf_counter()
+        fn()
+        first = time.perf_counter() - t0
+        for _ in range(4 if first < 0.2 else 0):
+            fn()
+        trials = 30 if first < 1.0 else 3
+        ts = []
+        for _ in range(trials):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return round(statistics.median(ts) * 1e3, 4)
+
+    X = np.ascontiguousarray(X, np.float32)
+    dY = np.ascontiguousarray(dY, np.float32)
+    return {"fwd": timeit(lambda: kern.fwd(W, X)), "dw": timeit(lambda: kern.dw(W, dY, X)),
+            "dx": timeit(lambda: kern.fwd(WT, dY)),
+            "transpose": timeit(lambda: O.transpose_with_perm(p)),
+            "kind": kern.kind, "transpose_kind": "port"}

@@ -43,6 +43,7 @@ class SlCsr(ctypes.Structure):
 SIGNATURES: dict[str, tuple] = {
     "sl_last_error": (ctypes.c_char_p, []),
     "sl_version": (ctypes.c_char_p, []),
+    "sl_last_kernel": (ctypes.c_char_p, []),
     "sl_device_status": (I32, [I32, P]),
     "sl_selftest_bounded_wait": (I32, [I64, P]),
     "sl_spmm_fwd": (I32, [P, P, I64, I64, P, P]),

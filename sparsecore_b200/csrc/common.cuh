@@ -13,6 +13,9 @@ namespace slb {
 
 // Per-host-thread error message behind sl_last_error().
 void set_error(const std::string& msg);
+// Records the kernel the last SpMM / SDDMM dispatch launched on this host
+// thread (a string literal), read back with sl_last_kernel().
+void note_kernel(const char* name);
 int fail(int code, const std::string& msg);
 // SL_OK, or SL_ERR_CUDA with the runtime's message prefixed by `what`.
 int cuda_status(cudaError_t e, const char* what);

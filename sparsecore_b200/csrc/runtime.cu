@@ -11,8 +11,10 @@
 namespace slb {
 
 thread_local std::string g_last_error;
+thread_local const char* g_last_kernel = "";
 
 void set_error(const std::string& msg) { g_last_error = msg; }
+void note_kernel(const char* name) { g_last_kernel = name; }
 
 int fail(int code, const std::string& msg) {
     g_last_error = msg;
@@ -190,6 +192,8 @@ using namespace slb;
 extern "C" {
 
 const char* sl_last_error(void) { return slb::g_last_error.c_str(); }
+
+const char* sl_last_kernel(void) { return slb::g_last_kernel; }
 
 const char* sl_version(void) { return "sparsecore_b200 0.1.0 (sm_100a)"; }
 

@@ -528,6 +528,7 @@ int launch_dw_n1(const sl_csr* W, const float* dY, const float* X, float* dW, cu
     int64_t blocks = (static_cast<int64_t>(M) + 7) / 8;
     const int64_t max_blocks = static_cast<int64_t>(num_sms()) * 8;
     if (blocks > max_blocks) blocks = max_blocks;
+    note_kernel("sddmm_n1_kernel");
     sddmm_n1_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
         M, W->row_start, W->row_nnz, W->row_capacity, W->col_indices, dY, X, dW);
     SL_RETURN_IF_LAUNCH_FAILED("sl_sddmm_dw (N = 1)");
@@ -567,6 +568,7 @@ int try_tiled(const sl_csr* W, const float* dY, const float* X, int64_t N, float
     int col_major = K > M ? 1 : 0;  // X (K x N) is the larger operand
     if (const char* e = std::getenv("SPARSECORE_B200_DW_ORDER"))  // row|col (measurements)
         col_major = e[0] == 'c' ? 1 : 0;
+    note_kernel("sddmm_tiled_kernel");
     kern<<<n_bi * n_bc, kTThreads + 32, smem, s>>>(
         dymap, xmap, static_cast<int>(M), N, TR, TC, n_bc, n_bi, col_major, W->row_start,
         W->row_nnz, W->row_capacity, W->col_indices, dW, status);
@@ -594,6 +596,7 @@ int launch_dw(const sl_csr* W, const float* dY, const float* X, int64_t N, float
     const int64_t max_blocks = static_cast<int64_t>(num_sms()) * 8;
     if (blocks > max_blocks) blocks = max_blocks;
     const bool vec4 = (N % 4 == 0) && aligned16(X) && aligned16(dY);
+    note_kernel(lane_kernel ? "sddmm_lane_kernel" : "sddmm_quad_kernel");
     if (lane_kernel) {
         if (vec4)
             sddmm_lane_kernel<true><<<static_cast<unsigned>(blocks), kDwThreads, 0, s>>>(

@@ -491,6 +491,7 @@ int launch_spmv_cfg(const sl_csr* W, const float* X, int64_t K, float* Y, cudaSt
                              static_cast<int>(smem)) != cudaSuccess)
         return -1;
     const int blocks = (M + 31) / 32;
+    note_kernel("spmv_lane_kernel");
     kern<<<blocks, 32, smem, s>>>(M, K, W->total_capacity, W->row_start, W->row_nnz,
                                   W->col_indices, W->values, X, Y);
     SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd (N = 1)");
@@ -622,6 +623,7 @@ int launch_lanerow_nv(const sl_csr* W, const float* X, float* Y, cudaStream_t s)
                              static_cast<int>(smem)) != cudaSuccess)
         return -1;
     const int M = static_cast<int>(W->nrows);
+    note_kernel("spmm_lanerow_kernel");
     spmm_lanerow_kernel<NV><<<(M + 31) / 32, 32, smem, s>>>(M, W->total_capacity, W->row_start,
                                                              W->row_nnz, W->col_indices, W->values, X, Y);
     SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd (lane per row)");
@@ -657,6 +659,7 @@ int launch_rowwarp(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStr
     int64_t blocks = (static_cast<int64_t>(M) + 7) / 8;
     const int64_t max_blocks = static_cast<int64_t>(num_sms()) * 8;
     if (blocks > max_blocks) blocks = max_blocks;
+    note_kernel("spmm_rowwarp_kernel");
     spmm_rowwarp_kernel<CPL, N1, FULL><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
         M, N, W->row_start, W->row_nnz, W->col_indices, W->values, X, Y);
     SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd");
@@ -688,6 +691,7 @@ int launch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_
     int64_t blocks = (n_items + wpb - 1) / wpb;
     const int64_t max_blocks = static_cast<int64_t>(sms) * (2048 / threads);
     if (blocks > max_blocks) blocks = max_blocks;
+    note_kernel("spmm_fwd_kernel");
     spmm_fwd_kernel<VEC, LPR, CPL><<<static_cast<unsigned>(blocks), threads, 0, s>>>(
         M, N, W->row_start, W->row_nnz, W->col_indices, W->values, X, Y, n_tiles, n_items);
     SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd");
@@ -876,6 +880,7 @@ int launch_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, c
     if (grid > n_items) grid = n_items;
     const int64_t per_cta = (n_items + grid - 1) / grid;
     grid = (n_items + per_cta - 1) / per_cta;
+    note_kernel("spmm_xs_kernel");
     spmm_xs_kernel<LPR><<<static_cast<unsigned>(grid), xs_threads<LPR>(), smem, s>>>(
         map, M, N, W->row_start, W->row_nnz, W->col_indices, W->values, Y, nbox, row_chunks,
         n_items, per_cta, status);

@@ -53,23 +53,14 @@ def oracle_csr(W):
 
 
 def launched_kernels(fn):
-    """Run ``fn`` under the CUDA activity profiler and return (its result,
-    the names of the GPU kernels it launched), so a parity test can assert
-    which kernel actually produced the values it checks."""
-    from torch.autograd import DeviceType
-    from torch.profiler import ProfilerActivity, profile
+    """Run ``fn`` and return (its result, [the kernel its last SpMM / SDDMM
+    dispatch launched]) as the library records it (sl_last_kernel), so a
+    parity test can assert which kernel produced the values it checks."""
+    from sparsecore_b200 import _native as N
 
-    out = fn()  # first call outside the profiler (one-time kernel attribute setup)
+    out = fn()
     torch.cuda.synchronize()
-    names = []
-    for _ in range(3):  # the activity trace occasionally comes back empty: retry
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            out = fn()
-            torch.cuda.synchronize()
-        names = [e.name for e in prof.events() if e.device_type == DeviceType.CUDA]
-        if names:
-            break
-    return out, names
+    return out, [N.lib().sl_last_kernel().decode()]
 
 
 def random_csr(M, K, density, seed, block=None, device=None):

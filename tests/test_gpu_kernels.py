@@ -236,8 +236,8 @@ def test_mid_n_sddmm_and_forward_vs_oracle(M, K, N, block, monkeypatch):
                                       (12000, 300, 0.9, 0.0), (7, 5, 0.3, 0.0), (4733, 1001, 0.8, 0.0),
                                       (300, 17000, 0.9, 0.2)])
 def test_spmv_lane_kernel_matches_oracle_and_warp_kernel(M, K, s, pr, monkeypatch):
-    """N = 1: forward / dX on the lane-per-row kernels (bulk-copied row
-    windows by default, both window sizes; the cp.async variant) and the
+    """N = 1: forward / dX on the lane-per-row kernels (cooperatively copied
+    row windows by default, both ring depths; the per-lane cp.async variant) and the
     streaming SDDMM, against the oracle and the general kernels: ragged and
     empty rows, rows whose 4-slot groups start unaligned or run past the
     arrays' end (no padding, total capacity not a multiple of 4), K above
@@ -265,11 +265,11 @@ def test_spmv_lane_kernel_matches_oracle_and_warp_kernel(M, K, s, pr, monkeypatc
     assert bits_equal(y, O.spmm(Wo, X.numpy()))
     assert bits_equal(dx, O.spmm(WTo, dY.numpy()))
     assert bits_equal(dw, O.sddmm(Wo, dY.numpy(), X.numpy()))
-    for win in ("64", "128"):  # both bulk-window configurations
-        monkeypatch.setenv("SPARSECORE_B200_N1_WIN", win)
-        assert bits_equal(sl.spmm(W, X.to(d)), y), win
-        assert bits_equal(ops._spmm_raw(WT, dY.to(d)), dx), win
-    monkeypatch.delenv("SPARSECORE_B200_N1_WIN")
+    for st in ("4", "8"):  # both window-ring configurations
+        monkeypatch.setenv("SPARSECORE_B200_N1_ST", st)
+        assert bits_equal(sl.spmm(W, X.to(d)), y), st
+        assert bits_equal(ops._spmm_raw(WT, dY.to(d)), dx), st
+    monkeypatch.delenv("SPARSECORE_B200_N1_ST")
     monkeypatch.setenv("SPARSECORE_B200_N1", "lane")  # the cp.async lane kernel
     assert bits_equal(sl.spmm(W, X.to(d)), y)
     assert bits_equal(ops._spmm_raw(WT, dY.to(d)), dx)
