@@ -202,7 +202,11 @@ spmm_fwd_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
 // (CPL of them).  With N = 1 each lane gathers X[col] of its pair one chunk
 // ahead and the buffer holds (value, x), so the chain costs half a shared
 // load and one FMA per slot.  Same FMA chain per element as above.
-template <int CPL, bool N1, bool FULL>
+// OFF32 (K * N < 2^31): the staged pair holds the X row's element offset
+// c * N instead of c, so each gather's address is one 32x32+64 multiply-add
+// from a per-lane base instead of 64-bit multiply, add and shift (those made
+// the N = 32 walk issue-bound at 11 instructions per slot).
+template <int CPL, bool N1, bool FULL, bool OFF32 = false>
 __global__ void __launch_bounds__(256)
 spmm_rowwarp_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
                     const int32_t* __restrict__ row_nnz, const int32_t* __restrict__ cols,
@@ -218,6 +222,10 @@ spmm_rowwarp_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
     int jcol[CPL];
 #pragma unroll
     for (int k = 0; k < CPL; ++k) jcol[k] = FULL ? lane + 32 * k : min(lane + 32 * k, static_cast<int>(N) - 1);
+    const float* xq[CPL];  // OFF32: per-lane column bases
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) xq[k] = X + jcol[k];
+    const int Ni = static_cast<int>(N);
     const int warps = gridDim.x * (blockDim.x >> 5);
     for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < M; row += warps) {
         const int rs = __ldg(row_start + row);
@@ -244,7 +252,7 @@ spmm_rowwarp_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
                     st[lane] = make_int2(__float_as_int(vr[j]), __float_as_int(xn));
                     xn = b + 32 + lane < nn ? __ldg(X + cr[(j + 1) % R]) : 0.0f;  // next chunk's gather
                 } else {
-                    st[lane] = make_int2(cr[j], __float_as_int(vr[j]));
+                    st[lane] = make_int2(OFF32 ? cr[j] * Ni : cr[j], __float_as_int(vr[j]));
                 }
                 const int k = b + 32 * R + lane;  // refill: chunk b + 32R
                 if (k < nn) {
@@ -293,8 +301,13 @@ spmm_rowwarp_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
                             for (int i = 0; i < G; ++i)
 #pragma unroll
                                 for (int q = 0; q < CPL; ++q) {
-                                    xa[i][q] = __ldg(X + static_cast<int64_t>(e[i].x) * N + jcol[q]);
-                                    xb[i][q] = __ldg(X + static_cast<int64_t>(e[i].z) * N + jcol[q]);
+                                    if constexpr (OFF32) {
+                                        xa[i][q] = __ldg(xq[q] + e[i].x);
+                                        xb[i][q] = __ldg(xq[q] + e[i].z);
+                                    } else {
+                                        xa[i][q] = __ldg(X + static_cast<int64_t>(e[i].x) * N + jcol[q]);
+                                        xb[i][q] = __ldg(X + static_cast<int64_t>(e[i].z) * N + jcol[q]);
+                                    }
                                 }
 #pragma unroll
                             for (int i = 0; i < G; ++i)
@@ -310,21 +323,28 @@ spmm_rowwarp_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
 #pragma unroll kUnroll
                     for (; t + 1 < cnt; t += 2) {
                         const int4 e = st4[t >> 1];
-                        const float* x0 = X + static_cast<int64_t>(e.x) * N;
-                        const float* x1 = X + static_cast<int64_t>(e.z) * N;
 #pragma unroll
                         for (int q = 0; q < CPL; ++q) {
-                            const float a0 = __ldg(x0 + jcol[q]), a1 = __ldg(x1 + jcol[q]);
+                            float a0, a1;
+                            if constexpr (OFF32) {
+                                a0 = __ldg(xq[q] + e.x);
+                                a1 = __ldg(xq[q] + e.z);
+                            } else {
+                                a0 = __ldg(X + static_cast<int64_t>(e.x) * N + jcol[q]);
+                                a1 = __ldg(X + static_cast<int64_t>(e.z) * N + jcol[q]);
+                            }
                             acc[q] = fmaf(__int_as_float(e.y), a0, acc[q]);
                             acc[q] = fmaf(__int_as_float(e.w), a1, acc[q]);
                         }
                     }
                     if (t < cnt) {
                         const int2 e = st[t];
-                        const float* x0 = X + static_cast<int64_t>(e.x) * N;
 #pragma unroll
-                        for (int q = 0; q < CPL; ++q)
-                            acc[q] = fmaf(__int_as_float(e.y), __ldg(x0 + jcol[q]), acc[q]);
+                        for (int q = 0; q < CPL; ++q) {
+                            const float a0 = OFF32 ? __ldg(xq[q] + e.x)
+                                                   : __ldg(X + static_cast<int64_t>(e.x) * N + jcol[q]);
+                            acc[q] = fmaf(__int_as_float(e.y), a0, acc[q]);
+                        }
                     }
                 }
                 __syncwarp();
@@ -653,14 +673,14 @@ bool spmv_lane_enabled(const sl_csr* W) {
     return aligned16(W->col_indices) && aligned16(W->values) && W->nrows > 0;
 }
 
-template <int CPL, bool N1, bool FULL = false>
+template <int CPL, bool N1, bool FULL = false, bool OFF32 = false>
 int launch_rowwarp(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_t s) {
     const int M = static_cast<int>(W->nrows);
     int64_t blocks = (static_cast<int64_t>(M) + 7) / 8;
     const int64_t max_blocks = static_cast<int64_t>(num_sms()) * 8;
     if (blocks > max_blocks) blocks = max_blocks;
     note_kernel("spmm_rowwarp_kernel");
-    spmm_rowwarp_kernel<CPL, N1, FULL><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+    spmm_rowwarp_kernel<CPL, N1, FULL, OFF32><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
         M, N, W->row_start, W->row_nnz, W->col_indices, W->values, X, Y);
     SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd");
     return SL_OK;
@@ -668,6 +688,15 @@ int launch_rowwarp(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStr
 
 int dispatch_rowwarp(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_t s) {
     if (N == 1) return launch_rowwarp<1, true>(W, X, N, Y, s);
+    if (W->ncols * N <= INT_MAX) {
+        if (N == 32) return launch_rowwarp<1, false, true, true>(W, X, N, Y, s);
+        if (N == 64) return launch_rowwarp<2, false, true, true>(W, X, N, Y, s);
+        if (N == 96) return launch_rowwarp<3, false, true, true>(W, X, N, Y, s);
+        if (N <= 32) return launch_rowwarp<1, false, false, true>(W, X, N, Y, s);
+        if (N <= 64) return launch_rowwarp<2, false, false, true>(W, X, N, Y, s);
+        if (N <= 96) return launch_rowwarp<3, false, false, true>(W, X, N, Y, s);
+        return launch_rowwarp<4, false, false, true>(W, X, N, Y, s);
+    }
     if (N == 32) return launch_rowwarp<1, false, true>(W, X, N, Y, s);
     if (N == 64) return launch_rowwarp<2, false, true>(W, X, N, Y, s);
     if (N == 96) return launch_rowwarp<3, false, true>(W, X, N, Y, s);
