@@ -19,8 +19,10 @@
 //    value 0).  X sits in shared memory with X[-1] = 0, so a neutral slot
 //    performs y = fma(0, 0, y) = y exactly (y is never -0: it starts at +0
 //    and a round-to-nearest sum is -0 only when both addends are -0).  The
-//    walk over a window is then predicate-free: per 4 slots two 128-bit
-//    shared loads (cols, values), four X loads and four FMAs;
+//    walk over a window is then predicate-free, in two passes: a gather
+//    pass replaces each col by X[col] in place (independent loads, many in
+//    flight), then the chain pass reads (value, x) as 128-bit pairs and
+//    runs at FMA latency;
 //  * row slices are WIN + 4 words apart, so the 8 lanes of a quarter-warp
 //    read distinct bank groups.
 // K above kMaxKs keeps X in global memory (read through L1, -1 -> 0).
@@ -85,21 +87,23 @@ spmv_coop_kernel(int M, int64_t K, int64_t cap_total, const int32_t* __restrict_
     const int NW = __reduce_max_sync(0xffffffffu, nw);
 
     // Copy window w of all 32 rows: lanes [kLpr*j, kLpr*j + kLpr) copy row
-    // rr + j, group li = lane % kLpr of the window.
+    // rr + j, group li = lane % kLpr of the window.  Slot indices fit in 32
+    // bits (row_start is int32), which keeps the address math short.
     const int sub = lane / kLpr, li = lane % kLpr;
+    const int a32 = static_cast<int>(a), ec32 = static_cast<int>(ecopy);
     auto issue = [&](int w) {
         const int b = w % ST;
-#pragma unroll 4
+        const int woff = w * kWin + 4 * li;
+        int* cdst = cring + b * S::kStageWords + sub * kStride + 4 * li;
+        float* vdst = vring + b * S::kStageWords + sub * kStride + 4 * li;
+#pragma unroll
         for (int rr = 0; rr < 32; rr += kRpi) {
             const int r = rr + sub;
-            const int64_t ra = __shfl_sync(0xffffffffu, a, r);
-            const int64_t re = __shfl_sync(0xffffffffu, ecopy, r);
-            const int64_t slot = ra + static_cast<int64_t>(w) * kWin + 4 * li;
-            const bool p = slot < re;
-            const int64_t src = p ? slot : 0;
-            const int dw = b * S::kStageWords + r * kStride + 4 * li;
-            cp16(cring + dw, cols + src, p);
-            cp16(vring + dw, vals + src, p);
+            const int slot = __shfl_sync(0xffffffffu, a32, r) + woff;
+            const bool p = slot < __shfl_sync(0xffffffffu, ec32, r);
+            const int src = p ? slot : 0;
+            cp16(cdst + rr * kStride, cols + src, p);
+            cp16(vdst + rr * kStride, vals + src, p);
         }
         cp_commit();
     };
@@ -142,26 +146,37 @@ spmv_coop_kernel(int M, int64_t K, int64_t cap_total, const int32_t* __restrict_
                 }
                 for (int64_t q = rs + nn; q < e && q < ecopy; ++q) { cb[q - s0] = -1; vb[q - s0] = 0.0f; }
             }
-            const int4* c4 = reinterpret_cast<const int4*>(cb);
-            const float4* v4 = reinterpret_cast<const float4*>(vb);
+            // Two passes over the window.  (1) Gather: X[c] replaces c in
+            // place -- groups are independent, so the loads of many groups
+            // are in flight together.  (2) The serial chain: per 4 slots two
+            // 128-bit loads (value, x) that do not depend on the chain, so
+            // they run ahead of it and the chain proceeds at FMA latency.
             const int ng = static_cast<int>(s1 - s0) >> 2;
-#pragma unroll 4
+            int4* c4 = reinterpret_cast<int4*>(cb);
+            float4* x4 = reinterpret_cast<float4*>(cb);
+            const float4* v4 = reinterpret_cast<const float4*>(vb);
+#pragma unroll 8
             for (int g = 0; g < ng; ++g) {
                 const int4 c = c4[g];
-                const float4 v = v4[g];
-                float x0, x1, x2, x3;
+                float4 x;
                 if (KS) {
-                    x0 = xs[c.x]; x1 = xs[c.y]; x2 = xs[c.z]; x3 = xs[c.w];
+                    x = make_float4(xs[c.x], xs[c.y], xs[c.z], xs[c.w]);
                 } else {
-                    x0 = c.x >= 0 ? __ldg(X + c.x) : 0.0f;
-                    x1 = c.y >= 0 ? __ldg(X + c.y) : 0.0f;
-                    x2 = c.z >= 0 ? __ldg(X + c.z) : 0.0f;
-                    x3 = c.w >= 0 ? __ldg(X + c.w) : 0.0f;
+                    x.x = c.x >= 0 ? __ldg(X + c.x) : 0.0f;
+                    x.y = c.y >= 0 ? __ldg(X + c.y) : 0.0f;
+                    x.z = c.z >= 0 ? __ldg(X + c.z) : 0.0f;
+                    x.w = c.w >= 0 ? __ldg(X + c.w) : 0.0f;
                 }
-                y = fmaf(v.x, x0, y);
-                y = fmaf(v.y, x1, y);
-                y = fmaf(v.z, x2, y);
-                y = fmaf(v.w, x3, y);
+                x4[g] = x;
+            }
+#pragma unroll 8
+            for (int g = 0; g < ng; ++g) {
+                const float4 x = x4[g];
+                const float4 v = v4[g];
+                y = fmaf(v.x, x.x, y);
+                y = fmaf(v.y, x.y, y);
+                y = fmaf(v.z, x.z, y);
+                y = fmaf(v.w, x.w, y);
             }
         }
         __syncwarp();  // every lane is done with buffer w % ST before it is refilled
