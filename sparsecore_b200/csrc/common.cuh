@@ -35,6 +35,13 @@ int row_grid(int64_t M);
 // N = 1 forward with per-lane bulk-copied row windows (spmv_bulk.cu);
 // -1 when it does not apply.
 int launch_spmv_bulk(const sl_csr* W, const float* X, int64_t K, float* Y, cudaStream_t s);
+// N = 32 forward / SDDMM with X rows staged by cp.async (gather32.cu); -1
+// when they do not apply.
+int launch_gather32_fwd(const sl_csr* W, const float* X, float* Y, cudaStream_t s);
+int launch_gather32_sddmm(const sl_csr* W, const float* dY, const float* X, float* dW,
+                          cudaStream_t s);
+// SPARSECORE_B200_N32=rows keeps N = 32 on the general kernels (tests).
+bool gather32_enabled();
 
 constexpr int kWarp = 32;
 

@@ -633,6 +633,10 @@ extern "C" int sl_sddmm_dw(const sl_csr* W, const float* dY, const float* X, int
         const char* e = std::getenv("SPARSECORE_B200_N1");
         if (e == nullptr || e[0] != 'w') return launch_dw_n1(W, dY, X, dW, s);
     }
+    if (N == 32 && W->ncols > 0 && gather32_enabled()) {
+        const int rc = launch_gather32_sddmm(W, dY, X, dW, s);
+        if (rc >= 0) return rc;
+    }
     if (!tiled_disabled() && W->ncols > 0) {
         const int rc = try_tiled(W, dY, X, N, dW, s);
         if (rc >= 0) return rc;

@@ -990,6 +990,10 @@ extern "C" int sl_spmm_fwd(const sl_csr* W, const float* X, int64_t K, int64_t N
         const int rc = try_lanerow(W, X, N, Y, s);
         if (rc >= 0) return rc;
     }
+    if (N == 32 && gather32_enabled()) {
+        const int rc = launch_gather32_fwd(W, X, Y, s);
+        if (rc >= 0) return rc;
+    }
     if (N < 128) return dispatch_rowwarp(W, X, N, Y, s);
     const bool vec4 = (N % 4 == 0) && aligned16(X) && aligned16(Y);
     return vec4 ? dispatch_fwd<4>(W, X, N, Y, s) : dispatch_fwd<1>(W, X, N, Y, s);

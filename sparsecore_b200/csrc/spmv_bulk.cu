@@ -29,6 +29,7 @@
 #include <cstdlib>
 
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace slb {
 namespace {
@@ -185,6 +186,194 @@ spmv_coop_kernel(int M, int64_t K, int64_t cap_total, const int32_t* __restrict_
     if (live) Y[row] = y;
 }
 
+// ── Warp-specialised variant ────────────────────────────────────────────
+// With few rows an SM runs a single warp of the kernel above, and one warp
+// cannot issue the copies, the gathers and the chain fast enough (about 9
+// instructions per slot at one instruction every few cycles).  Here a CTA
+// of three warps serves 32 rows: two producer warps (windows alternate
+// between them) copy a window cooperatively, apply the edge fix-ups and
+// replace each col by X[col] in place, and one consumer warp runs only the
+// chains -- per 4 slots two 128-bit loads and four FMAs, at FMA latency.
+// Stage s (window w % S) is handed over on full[s] (32 producer arrivals)
+// and back on empty[s] (one consumer arrival); every wait is bounded.
+// Windows: producer p owns w = p, p + 2, ...; it keeps D - 1 = S/2 - 1 of
+// them in flight and refills the stage of its window w - 2 once the
+// consumer has released it.
+template <int S, bool KS>
+__global__ void __launch_bounds__(96)
+spmv_ws_kernel(int M, int64_t K, int64_t cap_total, const int32_t* __restrict__ row_start,
+               const int32_t* __restrict__ row_nnz, const int32_t* __restrict__ cols,
+               const float* __restrict__ vals, const float* __restrict__ X,
+               float* __restrict__ Y, unsigned* status) {
+    static_assert(S % 2 == 0 && S >= 4, "two producers, at least two stages each");
+    constexpr int D = S / 2;
+    using SH = CoopShape<S>;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t full[S];
+    __shared__ __align__(8) uint64_t empty[S];
+    __shared__ __align__(8) uint64_t xbar;
+    int* cring = reinterpret_cast<int*>(smem_raw);
+    float* vring = reinterpret_cast<float*>(smem_raw + SH::kRing / 2);
+    float* xs = reinterpret_cast<float*>(smem_raw + SH::kXOff);
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int row = blockIdx.x * 32 + lane;
+    const bool live = row < M;
+    const int rs = live ? __ldg(row_start + row) : 0;
+    const int nn = live ? __ldg(row_nnz + row) : 0;
+    const int a = rs & ~3;
+    const int e = nn > 0 ? ((rs + nn + 3) & ~3) : a;
+    const int cap4 = static_cast<int>(cap_total & ~int64_t(3));
+    const int ecopy = e > cap4 ? cap4 : e;
+    const int nw = (e - a + kWin - 1) / kWin;
+    const int NW = __reduce_max_sync(0xffffffffu, nw);
+
+    if (threadIdx.x == 0) {
+        for (int b = 0; b < S; ++b) {
+            mbar_init(&full[b], 32);
+            mbar_init(&empty[b], 1);
+        }
+        mbar_init(&xbar, 32);
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    int* cslice = cring + lane * kStride;
+    float* vslice = vring + lane * kStride;
+    bool ok = true;
+
+    if (warp == 0) {  // consumer: X staging, then the chains
+        if (KS) {
+            if ((K % 4 == 0) && ((reinterpret_cast<uintptr_t>(X) & 15u) == 0)) {
+                for (int64_t k = 4 * lane; k < K; k += 128) cp16(xs + k, X + k, true);
+            } else {
+                for (int64_t k = lane; k < K; k += 32) xs[k] = __ldg(X + k);
+            }
+            if (lane == 0) xs[-1] = 0.0f;
+            cp_commit();
+            cp_wait<0>();
+        }
+        mbar_arrive(&xbar);
+        float y = 0.0f;
+        for (int w = 0; w < NW; ++w) {
+            const int b = w % S;
+            if (!mbar_wait(&full[b], static_cast<unsigned>((w / S) & 1), status)) { ok = false; break; }
+            if (w < nw) {
+                const int s0 = a + w * kWin;
+                const int ng = ((s0 + kWin < e ? s0 + kWin : e) - s0) >> 2;
+                const float4* x4 = reinterpret_cast<const float4*>(cslice + b * SH::kStageWords);
+                const float4* v4 = reinterpret_cast<const float4*>(vslice + b * SH::kStageWords);
+#pragma unroll 8
+                for (int g = 0; g < ng; ++g) {
+                    const float4 x = x4[g];
+                    const float4 v = v4[g];
+                    y = fmaf(v.x, x.x, y);
+                    y = fmaf(v.y, x.y, y);
+                    y = fmaf(v.z, x.z, y);
+                    y = fmaf(v.w, x.w, y);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[b]);
+        }
+        if (ok && live) Y[row] = y;
+        return;
+    }
+
+    // producers
+    const int p = warp - 1;
+    const int sub = lane / kLpr, li = lane % kLpr;
+    auto issue = [&](int w) {
+        const int b = w % S;
+        const int woff = w * kWin + 4 * li;
+        int* cdst = cring + b * SH::kStageWords + sub * kStride + 4 * li;
+        float* vdst = vring + b * SH::kStageWords + sub * kStride + 4 * li;
+#pragma unroll
+        for (int rr = 0; rr < 32; rr += kRpi) {
+            const int r = rr + sub;
+            const int slot = __shfl_sync(0xffffffffu, a, r) + woff;
+            const bool pr = slot < __shfl_sync(0xffffffffu, ecopy, r);
+            const int src = pr ? slot : 0;
+            cp16(cdst + rr * kStride, cols + src, pr);
+            cp16(vdst + rr * kStride, vals + src, pr);
+        }
+    };
+#pragma unroll
+    for (int i = 0; i < D - 1; ++i) {
+        const int w = p + 2 * i;
+        if (w < NW) issue(w);
+        cp_commit();
+    }
+    if (KS && !mbar_wait(&xbar, 0u, status)) ok = false;
+    for (int w = p; w < NW && ok; w += 2) {
+        const int b = w % S;
+        const int wn = w + 2 * (D - 1);  // refill: into the stage of window w - 2
+        if (wn < NW) {
+            if (w >= 2 && !mbar_wait(&empty[(w - 2) % S], static_cast<unsigned>(((w - 2) / S) & 1), status)) {
+                ok = false;
+                break;
+            }
+            issue(wn);
+        }
+        cp_commit();
+        cp_wait<D - 1>();  // this thread's copies of window w have landed
+        __syncwarp();      // ... and those of the other lanes of this warp
+        if (w < nw) {
+            int* cb = cslice + b * SH::kStageWords;
+            float* vb = vslice + b * SH::kStageWords;
+            const int s0 = a + w * kWin;
+            const int s1 = s0 + kWin < e ? s0 + kWin : e;
+            if (w == 0)
+                for (int q = a; q < rs; ++q) { cb[q - s0] = -1; vb[q - s0] = 0.0f; }
+            if (w == nw - 1) {
+                for (int q = ecopy > s0 ? ecopy : s0; q < e; ++q) {
+                    const bool in = q < rs + nn;
+                    cb[q - s0] = in ? __ldg(cols + q) : -1;
+                    vb[q - s0] = in ? __ldg(vals + q) : 0.0f;
+                }
+                for (int q = rs + nn; q < e && q < ecopy; ++q) { cb[q - s0] = -1; vb[q - s0] = 0.0f; }
+            }
+            int4* c4 = reinterpret_cast<int4*>(cb);
+            float4* x4 = reinterpret_cast<float4*>(cb);
+            const int ng = (s1 - s0) >> 2;
+#pragma unroll 8
+            for (int g = 0; g < ng; ++g) {
+                const int4 c = c4[g];
+                float4 x;
+                if (KS) {
+                    x = make_float4(xs[c.x], xs[c.y], xs[c.z], xs[c.w]);
+                } else {
+                    x.x = c.x >= 0 ? __ldg(X + c.x) : 0.0f;
+                    x.y = c.y >= 0 ? __ldg(X + c.y) : 0.0f;
+                    x.z = c.z >= 0 ? __ldg(X + c.z) : 0.0f;
+                    x.w = c.w >= 0 ? __ldg(X + c.w) : 0.0f;
+                }
+                x4[g] = x;
+            }
+        }
+        mbar_arrive(&full[b]);
+    }
+    cp_wait<0>();
+}
+
+template <int S, bool KS>
+int launch_ws(const sl_csr* W, const float* X, int64_t K, float* Y, cudaStream_t s) {
+    using SH = CoopShape<S>;
+    unsigned* status = device_status_word();
+    if (status == nullptr) return -1;
+    const size_t smem = SH::kXOff + (KS ? static_cast<size_t>(K) * 4 : 0);
+    auto kern = spmv_ws_kernel<S, KS>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+        return -1;
+    const int M = static_cast<int>(W->nrows);
+    note_kernel("spmv_ws_kernel");
+    kern<<<(M + 31) / 32, 96, smem, s>>>(M, K, W->total_capacity, W->row_start, W->row_nnz,
+                                         W->col_indices, W->values, X, Y, status);
+    SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd (N = 1, warp-specialised)");
+    return SL_OK;
+}
+
 template <int ST, bool KS>
 int launch_cfg(const sl_csr* W, const float* X, int64_t K, float* Y, cudaStream_t s) {
     using S = CoopShape<ST>;
@@ -205,11 +394,13 @@ int launch_cfg(const sl_csr* W, const float* X, int64_t K, float* Y, cudaStream_
 
 // At most one warp per SM: 8 windows in flight (one CTA per SM keeps about
 // 120 KB in flight).  More rows: 4 windows, two or more CTAs per SM.
-// SPARSECORE_B200_N1_ST=4|8 overrides (measurements).  Returns -1 when the
-// kernel cannot be configured (caller falls back).
+// SPARSECORE_B200_N1_ST=4|8 overrides the ring depth and
+// SPARSECORE_B200_N1_WS=0 selects the single-warp kernel (measurements and
+// tests).  Returns -1 when the kernel cannot be configured (caller falls
+// back).
 int launch_spmv_bulk(const sl_csr* W, const float* X, int64_t K, float* Y, cudaStream_t s) {
     if (!aligned16(W->col_indices) || !aligned16(W->values) || W->nrows <= 0 || K < 1 ||
-        W->nrows > INT_MAX - 32)
+        W->nrows > INT_MAX - 32 || W->total_capacity > INT_MAX - 4 * kWin * 16)
         return -1;
     const int64_t warps = (W->nrows + 31) / 32;
     int st = warps <= num_sms() ? 8 : 4;
@@ -217,7 +408,13 @@ int launch_spmv_bulk(const sl_csr* W, const float* X, int64_t K, float* Y, cudaS
         const int v = std::atoi(e);
         if (v == 4 || v == 8) st = v;
     }
+    bool ws = true;
+    if (const char* e = std::getenv("SPARSECORE_B200_N1_WS")) ws = e[0] != '0';
     const bool ks = K <= kMaxKs;
+    if (ws) {
+        if (st == 8) return ks ? launch_ws<8, true>(W, X, K, Y, s) : launch_ws<8, false>(W, X, K, Y, s);
+        return ks ? launch_ws<4, true>(W, X, K, Y, s) : launch_ws<4, false>(W, X, K, Y, s);
+    }
     if (st == 8) return ks ? launch_cfg<8, true>(W, X, K, Y, s) : launch_cfg<8, false>(W, X, K, Y, s);
     return ks ? launch_cfg<4, true>(W, X, K, Y, s) : launch_cfg<4, false>(W, X, K, Y, s);
 }

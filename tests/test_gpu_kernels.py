@@ -265,11 +265,14 @@ def test_spmv_lane_kernel_matches_oracle_and_warp_kernel(M, K, s, pr, monkeypatc
     assert bits_equal(y, O.spmm(Wo, X.numpy()))
     assert bits_equal(dx, O.spmm(WTo, dY.numpy()))
     assert bits_equal(dw, O.sddmm(Wo, dY.numpy(), X.numpy()))
-    for st in ("4", "8"):  # both window-ring configurations
-        monkeypatch.setenv("SPARSECORE_B200_N1_ST", st)
-        assert bits_equal(sl.spmm(W, X.to(d)), y), st
-        assert bits_equal(ops._spmm_raw(WT, dY.to(d)), dx), st
+    for ws in ("1", "0"):  # warp-specialised and single-warp window kernels
+        monkeypatch.setenv("SPARSECORE_B200_N1_WS", ws)
+        for st in ("4", "8"):  # both ring depths
+            monkeypatch.setenv("SPARSECORE_B200_N1_ST", st)
+            assert bits_equal(sl.spmm(W, X.to(d)), y), (ws, st)
+            assert bits_equal(ops._spmm_raw(WT, dY.to(d)), dx), (ws, st)
     monkeypatch.delenv("SPARSECORE_B200_N1_ST")
+    monkeypatch.delenv("SPARSECORE_B200_N1_WS")
     monkeypatch.setenv("SPARSECORE_B200_N1", "lane")  # the cp.async lane kernel
     assert bits_equal(sl.spmm(W, X.to(d)), y)
     assert bits_equal(ops._spmm_raw(WT, dY.to(d)), dx)
@@ -311,3 +314,43 @@ def test_lanerow_small_n_matches_oracle_and_warp_kernel(M, K, s, pr, monkeypatch
         assert bits_equal(sl.spmm(W, X.to(d)), y), N
         assert bits_equal(ops._spmm_raw(WT, dY.to(d)), dx), N
         monkeypatch.delenv("SPARSECORE_B200_SMALLN")
+
+
+@pytest.mark.parametrize("M,K,s", [(301, 517, 0.9), (2000, 4096, 0.95), (50, 70, 0.0)])
+def test_n32_gather_kernels_vs_oracle(M, K, s, monkeypatch):
+    """N = 32: the forward / dX and SDDMM kernels that stage X rows by
+    cp.async, against the oracle and the general kernels: empty rows, rows of
+    exactly 32 / 33 / 64 slots (chunk edges) and one long row, so the
+    register ring and the staging ring both wrap."""
+    import sparsecore_b200 as sl
+    from oracle import oracle as O
+    from sparsecore_b200 import ops
+
+    from gpu_helpers import launched_kernels
+
+    d = dev()
+    g = torch.Generator().manual_seed(M + K)
+    mask = torch.rand(M, K, generator=g) >= s
+    mask[1] = False
+    if M > 10:
+        for r, n in ((2, 32), (3, 33), (4, 64), (5, 31)):
+            mask[r] = False
+            mask[r, :n] = True
+        mask[M // 2] = True  # a long row: many chunks
+    W = sl.PaddedCSR.from_dense((torch.randn(M, K, generator=g) * mask).to(d))
+    Wo = oracle_csr(W)
+    WT, _ = sl.transpose_with_perm(W)
+    WTo, _ = O.transpose_with_perm(Wo)
+    X = torch.randn(K, 32, generator=g)
+    dY = torch.randn(M, 32, generator=g)
+    y, names = launched_kernels(lambda: sl.spmm(W, X.to(d)))
+    assert names == ["gather32_fwd_kernel"], names
+    dw, names = launched_kernels(lambda: ops._sddmm_raw(W, dY.to(d), X.to(d)))
+    assert names == ["gather32_sddmm_kernel"], names
+    dx = ops._spmm_raw(WT, dY.to(d))
+    assert bits_equal(y, O.spmm(Wo, X.numpy()))
+    assert bits_equal(dw, O.sddmm(Wo, dY.numpy(), X.numpy()))
+    assert bits_equal(dx, O.spmm(WTo, dY.numpy()))
+    monkeypatch.setenv("SPARSECORE_B200_N32", "rows")
+    assert bits_equal(sl.spmm(W, X.to(d)), y)
+    assert bits_equal(ops._sddmm_raw(W, dY.to(d), X.to(d)), dw)
