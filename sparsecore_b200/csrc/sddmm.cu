@@ -492,8 +492,11 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
 // FMA of the scalar tail onto the +0 horizontal sum), so the SDDMM is a
 // stream over the slot arrays: one warp per row writes the row's whole
 // capacity (live slots and zeroed padding) with coalesced loads of the
-// column indices and coalesced stores, four 32-slot strips in flight per
-// warp, X gathered through L1.
+// column indices and coalesced stores, X gathered through L1.  A warp keeps
+// the next round's column loads in flight while it gathers and stores the
+// current one (U strips of 32 slots per round), so each SM has tens of KB of
+// loads outstanding.
+constexpr int kN1U = 8;
 __global__ void __launch_bounds__(256)
 sddmm_n1_kernel(int M, const int32_t* __restrict__ row_start, const int32_t* __restrict__ row_nnz,
                 const int32_t* __restrict__ row_capacity, const int32_t* __restrict__ cols,
@@ -504,21 +507,29 @@ sddmm_n1_kernel(int M, const int32_t* __restrict__ row_start, const int32_t* __r
         const int rs = __ldg(row_start + row), nn = __ldg(row_nnz + row);
         const int cp = __ldg(row_capacity + row);
         const float dy = __ldg(dY + row);
-        for (int k0 = 0; k0 < cp; k0 += 128) {
-            int c[4];
+        int c[kN1U];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int k = k0 + 32 * u + lane;
-                c[u] = k < nn ? __ldg(cols + rs + k) : -1;
+        for (int u = 0; u < kN1U; ++u) {
+            const int k = 32 * u + lane;
+            c[u] = k < nn ? __ldg(cols + rs + k) : -1;
+        }
+        for (int k0 = 0; k0 < cp; k0 += 32 * kN1U) {
+            int cn[kN1U];  // next round's columns, in flight during this round's work
+#pragma unroll
+            for (int u = 0; u < kN1U; ++u) {
+                const int k = k0 + 32 * (kN1U + u) + lane;
+                cn[u] = k < nn ? __ldg(cols + rs + k) : -1;
             }
-            float x[4];
+            float x[kN1U];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) x[u] = c[u] >= 0 ? __ldg(X + c[u]) : 0.0f;
+            for (int u = 0; u < kN1U; ++u) x[u] = c[u] >= 0 ? __ldg(X + c[u]) : 0.0f;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < kN1U; ++u) {
                 const int k = k0 + 32 * u + lane;
                 if (k < cp) dW[rs + k] = c[u] >= 0 ? fmaf(dy, x[u], 0.0f) : 0.0f;
             }
+#pragma unroll
+            for (int u = 0; u < kN1U; ++u) c[u] = cn[u];
         }
     }
 }
