@@ -395,13 +395,24 @@ def run_ours(args, rank, world, local_rank):
     batch_host = tuple(t.pin_memory() for t in wl.batch)
     batch_dev = tuple(t.to(dev) for t in batch_host)
 
+    ar_events = []  # (start, end) around the gradient exchange, serial pass only
+
     def train(*batch):
         opt.zero_grad(set_to_none=True)
         loss = wl.loss_fn(model, batch)
         loss.backward()
-        ddp.allreduce_grads()
+        if timing_exchange["on"]:
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record()
+            ddp.allreduce_grads()
+            a1.record()
+            ar_events.append((a0, a1))
+        else:
+            ddp.allreduce_grads()
         opt.step()
         return loss
+
+    timing_exchange = {"on": False}
 
     def route():
         algo.step()
@@ -459,13 +470,16 @@ def run_ours(args, rank, world, local_rank):
     timed_steps = min(args.steps, 5)
     ops.set_async_weight_grad(False)
     ops.set_kernel_timer(timer)
+    timing_exchange["on"] = True
     s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s0.record()
     for _ in range(timed_steps):
         train(*batch_dev)
     s1.record()
     torch.cuda.synchronize()
+    timing_exchange["on"] = False
     serial_ms = s0.elapsed_time(s1) / timed_steps
+    exchange_ms = (sum(a.elapsed_time(b) for a, b in ar_events) / len(ar_events)) if ar_events else 0.0
     ops.set_kernel_timer(None)
     ops.set_async_weight_grad(True)
     ksum = timer.summary()
@@ -502,10 +516,10 @@ def run_ours(args, rank, world, local_rank):
     # kernel's output would have been incomplete).
     N.check_device_status(dev)
 
-    t = torch.tensor([t_ms, e2e_ms, router_ms], device=dev, dtype=torch.float64)
+    t = torch.tensor([t_ms, e2e_ms, router_ms, exchange_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    t_ms, e2e_ms, router_ms = t.tolist()
+    t_ms, e2e_ms, router_ms, exchange_ms = t.tolist()
     if rank != 0:
         return None
 
@@ -552,6 +566,13 @@ def run_ours(args, rank, world, local_rank):
                        if graphed is not None else None),
         "clocks": clk,
         "device_status": "clean: no bounded device wait timed out (checked after the run)",
+        "gradient_exchange": {
+            "bucket_bytes": ddp.bucket_numel * 4,
+            "ms_per_step": round(exchange_ms, 3),
+            "share_of_step": round(exchange_ms / (t_ms / args.steps), 4),
+            "what": ("pack live dW slots + dense grads into one fp32 bucket, NCCL all-reduce "
+                     "(AVG), unpack; CUDA events around allreduce_grads() in the serial pass, "
+                     "max over ranks") if world > 1 else "single GPU: no exchange"},
         "router": {"algorithm": type(algo).__name__, "every_steps": algo.update_freq,
                    "update_plus_broadcast_ms": round(router_ms, 1),
                    "note": "no update falls inside the timed window; amortised cost per step = "
@@ -670,6 +691,11 @@ def main():
         line = run_reference(args, rank, world)
     else:
         if world > 1:
+            # NCCL's communicator set-up lines (ranks, transport) on stderr;
+            # stdout keeps the one JSON line.
+            os.environ.setdefault("NCCL_DEBUG", "INFO")
+            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+            os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
             torch.cuda.set_device(local_rank)
             dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
         line = run_ours(args, rank, world, local_rank)

@@ -191,30 +191,44 @@ spmv_coop_kernel(int M, int64_t K, int64_t cap_total, const int32_t* __restrict_
 // cannot issue the copies, the gathers and the chain fast enough (about 9
 // instructions per slot at one instruction every few cycles).  Here a CTA
 // of three warps serves 32 rows: two producer warps (windows alternate
-// between them) copy a window cooperatively, apply the edge fix-ups and
-// replace each col by X[col] in place, and one consumer warp runs only the
-// chains -- per 4 slots two 128-bit loads and four FMAs, at FMA latency.
+// between them) bring a window in, apply the edge fix-ups and replace each
+// col by X[col] in place, and one consumer warp runs only the chains -- per
+// 4 slots two 128-bit loads and four FMAs, at FMA latency.
+// Copies: BULK = one 1-D bulk copy (cp.async.bulk, no multicast) per row and
+// array per window, posted on the stage's mbarrier by the row's producer
+// lane: the copy engine keeps them in flight without the L1 miss-tracking
+// limit that caps cp.async and plain loads at a few tens of KB per SM.
+// Otherwise the warp copies cooperatively with 16-byte cp.async as above.
 // Stage s (window w % S) is handed over on full[s] (32 producer arrivals)
 // and back on empty[s] (one consumer arrival); every wait is bounded.
-// Windows: producer p owns w = p, p + 2, ...; it keeps D - 1 = S/2 - 1 of
+// Producer p owns windows w = p, p + 2, ...; it keeps D - 1 = S/2 - 1 of
 // them in flight and refills the stage of its window w - 2 once the
 // consumer has released it.
-template <int S, bool KS>
-__global__ void __launch_bounds__(96)
+template <int WIN>
+struct WsShape {
+    static constexpr int kStride = WIN + 4;                 // words per row slice
+    static constexpr int kStageWords = 32 * kStride;        // one array, one stage
+};
+
+template <int WIN, int S, bool KS, bool BULK>
+__global__ void __launch_bounds__(96, 1)
 spmv_ws_kernel(int M, int64_t K, int64_t cap_total, const int32_t* __restrict__ row_start,
                const int32_t* __restrict__ row_nnz, const int32_t* __restrict__ cols,
                const float* __restrict__ vals, const float* __restrict__ X,
                float* __restrict__ Y, unsigned* status) {
     static_assert(S % 2 == 0 && S >= 4, "two producers, at least two stages each");
     constexpr int D = S / 2;
-    using SH = CoopShape<S>;
+    constexpr int kStr = WsShape<WIN>::kStride;
+    constexpr int kSW = WsShape<WIN>::kStageWords;
+    constexpr size_t kRing = size_t(S) * kSW * 4 * 2;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t full[S];
     __shared__ __align__(8) uint64_t empty[S];
+    __shared__ __align__(8) uint64_t landed[S];
     __shared__ __align__(8) uint64_t xbar;
     int* cring = reinterpret_cast<int*>(smem_raw);
-    float* vring = reinterpret_cast<float*>(smem_raw + SH::kRing / 2);
-    float* xs = reinterpret_cast<float*>(smem_raw + SH::kXOff);
+    float* vring = reinterpret_cast<float*>(smem_raw + kRing / 2);
+    float* xs = reinterpret_cast<float*>(smem_raw + kRing + 16);
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int row = blockIdx.x * 32 + lane;
@@ -225,21 +239,22 @@ spmv_ws_kernel(int M, int64_t K, int64_t cap_total, const int32_t* __restrict__ 
     const int e = nn > 0 ? ((rs + nn + 3) & ~3) : a;
     const int cap4 = static_cast<int>(cap_total & ~int64_t(3));
     const int ecopy = e > cap4 ? cap4 : e;
-    const int nw = (e - a + kWin - 1) / kWin;
+    const int nw = (e - a + WIN - 1) / WIN;
     const int NW = __reduce_max_sync(0xffffffffu, nw);
 
     if (threadIdx.x == 0) {
         for (int b = 0; b < S; ++b) {
             mbar_init(&full[b], 32);
             mbar_init(&empty[b], 1);
+            mbar_init(&landed[b], 32);
         }
         mbar_init(&xbar, 32);
         fence_barrier_init();
     }
     __syncthreads();
 
-    int* cslice = cring + lane * kStride;
-    float* vslice = vring + lane * kStride;
+    int* cslice = cring + lane * kStr;
+    float* vslice = vring + lane * kStr;
     bool ok = true;
 
     if (warp == 0) {  // consumer: X staging, then the chains
@@ -259,10 +274,10 @@ spmv_ws_kernel(int M, int64_t K, int64_t cap_total, const int32_t* __restrict__ 
             const int b = w % S;
             if (!mbar_wait(&full[b], static_cast<unsigned>((w / S) & 1), status)) { ok = false; break; }
             if (w < nw) {
-                const int s0 = a + w * kWin;
-                const int ng = ((s0 + kWin < e ? s0 + kWin : e) - s0) >> 2;
-                const float4* x4 = reinterpret_cast<const float4*>(cslice + b * SH::kStageWords);
-                const float4* v4 = reinterpret_cast<const float4*>(vslice + b * SH::kStageWords);
+                const int s0 = a + w * WIN;
+                const int ng = ((s0 + WIN < e ? s0 + WIN : e) - s0) >> 2;
+                const float4* x4 = reinterpret_cast<const float4*>(cslice + b * kSW);
+                const float4* v4 = reinterpret_cast<const float4*>(vslice + b * kSW);
 #pragma unroll 8
                 for (int g = 0; g < ng; ++g) {
                     const float4 x = x4[g];
@@ -282,27 +297,59 @@ spmv_ws_kernel(int M, int64_t K, int64_t cap_total, const int32_t* __restrict__ 
 
     // producers
     const int p = warp - 1;
-    const int sub = lane / kLpr, li = lane % kLpr;
     auto issue = [&](int w) {
         const int b = w % S;
-        const int woff = w * kWin + 4 * li;
-        int* cdst = cring + b * SH::kStageWords + sub * kStride + 4 * li;
-        float* vdst = vring + b * SH::kStageWords + sub * kStride + 4 * li;
+        if constexpr (BULK) {
+            unsigned bytes = 0;
+            int s0 = 0;
+            if (w < nw) {
+                s0 = a + w * WIN;
+                const int s1 = s0 + WIN < ecopy ? s0 + WIN : ecopy;
+                if (s1 > s0) bytes = static_cast<unsigned>(s1 - s0) * 4u;
+            }
+            if (bytes) {
+                mbar_expect_tx(&landed[b], 2 * bytes);
+                bulk_load_1d(cslice + b * kSW, cols + s0, bytes, &landed[b]);
+                bulk_load_1d(vslice + b * kSW, vals + s0, bytes, &landed[b]);
+            } else {
+                mbar_arrive(&landed[b]);
+            }
+        } else {
+            constexpr int LPR = WIN / 4 < 32 ? WIN / 4 : 32;  // lanes per row
+            constexpr int RPI = 32 / LPR;                     // rows per instruction
+            const int sub = lane / LPR, li = lane % LPR;
+            int* cdst = cring + b * kSW + sub * kStr + 4 * li;
+            float* vdst = vring + b * kSW + sub * kStr + 4 * li;
+#pragma unroll 4
+            for (int rr = 0; rr < 32; rr += RPI) {
+                const int r = rr + sub;
+                const int ra = __shfl_sync(0xffffffffu, a, r);
+                const int re = __shfl_sync(0xffffffffu, ecopy, r);
 #pragma unroll
-        for (int rr = 0; rr < 32; rr += kRpi) {
-            const int r = rr + sub;
-            const int slot = __shfl_sync(0xffffffffu, a, r) + woff;
-            const bool pr = slot < __shfl_sync(0xffffffffu, ecopy, r);
-            const int src = pr ? slot : 0;
-            cp16(cdst + rr * kStride, cols + src, pr);
-            cp16(vdst + rr * kStride, vals + src, pr);
+                for (int h = 0; h < WIN / (4 * LPR); ++h) {
+                    const int slot = ra + w * WIN + 4 * (li + LPR * h);
+                    const bool pr = slot < re;
+                    const int src = pr ? slot : 0;
+                    cp16(cdst + rr * kStr + 4 * LPR * h, cols + src, pr);
+                    cp16(vdst + rr * kStr + 4 * LPR * h, vals + src, pr);
+                }
+            }
+            cp_commit();
+        }
+    };
+    auto landed_wait = [&](int w) -> bool {
+        if constexpr (BULK) {
+            return mbar_wait(&landed[w % S], static_cast<unsigned>((w / S) & 1), status);
+        } else {
+            cp_wait<D - 1>();
+            return true;
         }
     };
 #pragma unroll
     for (int i = 0; i < D - 1; ++i) {
         const int w = p + 2 * i;
         if (w < NW) issue(w);
-        cp_commit();
+        else if (!BULK) cp_commit();
     }
     if (KS && !mbar_wait(&xbar, 0u, status)) ok = false;
     for (int w = p; w < NW && ok; w += 2) {
@@ -313,16 +360,18 @@ spmv_ws_kernel(int M, int64_t K, int64_t cap_total, const int32_t* __restrict__ 
                 ok = false;
                 break;
             }
+            if (BULK) fence_proxy_async();  // this warp's gather writes -> the copy engine's
             issue(wn);
+        } else if (!BULK) {
+            cp_commit();
         }
-        cp_commit();
-        cp_wait<D - 1>();  // this thread's copies of window w have landed
-        __syncwarp();      // ... and those of the other lanes of this warp
+        if (!landed_wait(w)) { ok = false; break; }
+        __syncwarp();  // every lane's copies of window w are visible
         if (w < nw) {
-            int* cb = cslice + b * SH::kStageWords;
-            float* vb = vslice + b * SH::kStageWords;
-            const int s0 = a + w * kWin;
-            const int s1 = s0 + kWin < e ? s0 + kWin : e;
+            int* cb = cslice + b * kSW;
+            float* vb = vslice + b * kSW;
+            const int s0 = a + w * WIN;
+            const int s1 = s0 + WIN < e ? s0 + WIN : e;
             if (w == 0)
                 for (int q = a; q < rs; ++q) { cb[q - s0] = -1; vb[q - s0] = 0.0f; }
             if (w == nw - 1) {
@@ -353,16 +402,20 @@ spmv_ws_kernel(int M, int64_t K, int64_t cap_total, const int32_t* __restrict__ 
         }
         mbar_arrive(&full[b]);
     }
-    cp_wait<0>();
+    if (!ok && BULK) {
+        // A wait gave up: let this warp's issued copies land (bounded) before exiting.
+        for (int w = p; w < NW; w += 2) mbar_wait(&landed[w % S], static_cast<unsigned>((w / S) & 1), status, 1 << 12);
+    }
+    if (!BULK) cp_wait<0>();
 }
 
-template <int S, bool KS>
+template <int WIN, int S, bool KS, bool BULK>
 int launch_ws(const sl_csr* W, const float* X, int64_t K, float* Y, cudaStream_t s) {
-    using SH = CoopShape<S>;
     unsigned* status = device_status_word();
     if (status == nullptr) return -1;
-    const size_t smem = SH::kXOff + (KS ? static_cast<size_t>(K) * 4 : 0);
-    auto kern = spmv_ws_kernel<S, KS>;
+    const size_t smem = size_t(S) * WsShape<WIN>::kStageWords * 4 * 2 + 16 +
+                        (KS ? static_cast<size_t>(K) * 4 : 0);
+    auto kern = spmv_ws_kernel<WIN, S, KS, BULK>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
         return -1;
@@ -408,12 +461,20 @@ int launch_spmv_bulk(const sl_csr* W, const float* X, int64_t K, float* Y, cudaS
         const int v = std::atoi(e);
         if (v == 4 || v == 8) st = v;
     }
-    bool ws = true;
-    if (const char* e = std::getenv("SPARSECORE_B200_N1_WS")) ws = e[0] != '0';
+    // SPARSECORE_B200_N1_WS=0: single-warp kernel; =1: warp-specialised with
+    // cp.async copies; default (=2): warp-specialised with bulk copies of
+    // 128-slot windows, 6 stages (4 when X takes 64 KB of shared memory).
+    int ws = 2;
+    if (const char* e = std::getenv("SPARSECORE_B200_N1_WS")) ws = e[0] - '0';
     const bool ks = K <= kMaxKs;
-    if (ws) {
-        if (st == 8) return ks ? launch_ws<8, true>(W, X, K, Y, s) : launch_ws<8, false>(W, X, K, Y, s);
-        return ks ? launch_ws<4, true>(W, X, K, Y, s) : launch_ws<4, false>(W, X, K, Y, s);
+    if (ws == 2) {
+        const bool deep = !ks || K <= 4096;
+        if (deep) return ks ? launch_ws<128, 6, true, true>(W, X, K, Y, s) : launch_ws<128, 6, false, true>(W, X, K, Y, s);
+        return launch_ws<128, 4, true, true>(W, X, K, Y, s);
+    }
+    if (ws == 1) {
+        if (st == 8) return ks ? launch_ws<64, 8, true, false>(W, X, K, Y, s) : launch_ws<64, 8, false, false>(W, X, K, Y, s);
+        return ks ? launch_ws<64, 4, true, false>(W, X, K, Y, s) : launch_ws<64, 4, false, false>(W, X, K, Y, s);
     }
     if (st == 8) return ks ? launch_cfg<8, true>(W, X, K, Y, s) : launch_cfg<8, false>(W, X, K, Y, s);
     return ks ? launch_cfg<4, true>(W, X, K, Y, s) : launch_cfg<4, false>(W, X, K, Y, s);

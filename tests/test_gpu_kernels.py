@@ -265,7 +265,7 @@ def test_spmv_lane_kernel_matches_oracle_and_warp_kernel(M, K, s, pr, monkeypatc
     assert bits_equal(y, O.spmm(Wo, X.numpy()))
     assert bits_equal(dx, O.spmm(WTo, dY.numpy()))
     assert bits_equal(dw, O.sddmm(Wo, dY.numpy(), X.numpy()))
-    for ws in ("1", "0"):  # warp-specialised and single-warp window kernels
+    for ws in ("2", "1", "0"):  # warp-specialised (bulk / cp.async copies), single-warp
         monkeypatch.setenv("SPARSECORE_B200_N1_WS", ws)
         for st in ("4", "8"):  # both ring depths
             monkeypatch.setenv("SPARSECORE_B200_N1_ST", st)
