@@ -176,10 +176,14 @@ def graph_time_ms(fn, flush_buf, reps=10):
 def run_sweep(args):
     """Config 3: W in {4096x4096, 16384x4096} x sparsity x N; fwd, SDDMM, dX."""
     import sparsecore_b200 as sl
+    from sparsecore_b200 import _native as N
     from sparsecore_b200 import ops
 
     hbm, src, sm_max = peaks()
-    fp32 = 148 * 128 * 2 * sm_max * 1e6 / 1e12
+    ceil = N.measure_ceilings()
+    fp32 = ceil["fp32_tflops"]
+    gather = ceil["gather_ceiling_tflops"]
+    print(json.dumps({"measured_ceilings": ceil, "hbm_gbs": hbm, "hbm_source": src}), flush=True)
 
     flush_buf = torch.zeros(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MB > L2
 
@@ -216,6 +220,7 @@ def run_sweep(args):
                     cell[kind] = {"ms": round(ms, 4), "GB/s": round(gbs, 1),
                                   "hbm_frac": round(gbs / hbm, 3), "TFLOP/s": round(tfl, 2),
                                   "fp32_frac": round(tfl / fp32, 3),
+                                  "gather_frac": round(tfl / gather, 3),
                                   "bound": "hbm" if hbm_floor >= fma_floor else "fp32-fma",
                                   "binding_frac": round(max(hbm_floor, fma_floor) / ms, 3)}
                 if 0 < N <= args.sweep_cpu_max_n:
@@ -388,6 +393,7 @@ def run_ours(args, rank, world, local_rank):
         from sparsecore_b200.ops import critical_path_stream
 
         torch.cuda.set_stream(critical_path_stream(dev))
+    ceil = N.measure_ceilings(dev)  # before the workload, on an idle GPU
     wl = Workload(args.workload, dev, rank, capturable=args.graph)
     model, algo, opt = wl.model, wl.algo, wl.opt
     ops.set_async_weight_grad(True)  # the loop below reads .grad after backward()
@@ -531,7 +537,7 @@ def run_ours(args, rank, world, local_rank):
         d = ksum[dom]
         gbs = d["bytes"] / (d["ms"] * 1e-3) / 1e9
         tfl = d["flops"] / (d["ms"] * 1e-3) / 1e12
-        fp32_peak = 148 * 128 * 2 * sm_max * 1e6 / 1e12
+        fp32_peak = ceil["fp32_tflops"]
         roof = {"bound": "hbm", "kernel": dom, "achieved": round(gbs, 1), "peak": hbm,
                 "unit": "GB/s", "frac": round(gbs / hbm, 4), "peak_source": f"{hbm_src} (MEASURED_PEAKS.json hbm_gbs)",
                 "traffic": read_traffic(dom), "launches": d["launches"],
@@ -539,6 +545,9 @@ def run_ours(args, rank, world, local_rank):
                 "achieved_fp32_tflops": round(tfl, 2),
                 "fp32_fma_peak_tflops": round(fp32_peak, 1),
                 "fp32_frac": round(tfl / fp32_peak, 4),
+                "gather_ceiling_tflops": ceil["gather_ceiling_tflops"],
+                "gather_frac": round(tfl / ceil["gather_ceiling_tflops"], 4),
+                "ceilings": ceil,
                 "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 2),
                                 "GB/s": round(v["bytes"] / (v["ms"] * 1e-3) / 1e9, 1),
                                 "TFLOP/s": round(v["flops"] / (v["ms"] * 1e-3) / 1e12, 2)}

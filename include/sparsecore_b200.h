@@ -58,6 +58,16 @@ SL_API const char* sl_last_error(void);
  * host thread launched (a diagnostic with no reference counterpart: tests
  * use it to prove which decomposition produced the values they check). */
 SL_API const char* sl_last_kernel(void);
+/* Roofline probes (no reference counterpart): sl_probe_ffma runs
+ * sl_probe_threads() threads, each advancing 8 independent fp32 FMA chains
+ * for `iters` steps (16 * iters FLOPs per thread); sl_probe_smem has the same
+ * threads each read `iters` conflict-free 16-byte shared-memory words.
+ * `out` receives one float per thread (sl_probe_threads() floats).  Timed by
+ * the caller (CUDA events) to give the measured FP32 and shared-memory
+ * ceilings the kernels' fractions are reported against. */
+SL_API int64_t sl_probe_threads(void);
+SL_API int sl_probe_ffma(int64_t iters, float* out, void* stream);
+SL_API int sl_probe_smem(int64_t iters, float* out, void* stream);
 /* Library version string. */
 SL_API const char* sl_version(void);
 /* Status word of the current device (synchronous): bit 0 set = a bounded

@@ -44,6 +44,9 @@ SIGNATURES: dict[str, tuple] = {
     "sl_last_error": (ctypes.c_char_p, []),
     "sl_version": (ctypes.c_char_p, []),
     "sl_last_kernel": (ctypes.c_char_p, []),
+    "sl_probe_threads": (I64, []),
+    "sl_probe_ffma": (I32, [I64, P, P]),
+    "sl_probe_smem": (I32, [I64, P, P]),
     "sl_device_status": (I32, [I32, P]),
     "sl_selftest_bounded_wait": (I32, [I64, P]),
     "sl_spmm_fwd": (I32, [P, P, I64, I64, P, P]),
@@ -140,6 +143,7 @@ KERNELS_PER_CALL = {
     "sl_dst_keep": 1, "sl_dst_apply_random": 1, "sl_dst_apply_topk": 1, "sl_dst_apply_cols": 1,
     "sl_pack_live": 1, "sl_unpack_live": 1, "sl_exclusive_scan": 1,
     "sl_set_regrow_draws": 0,  # host only
+    "sl_probe_ffma": 1, "sl_probe_smem": 1,
 }
 launches = {"count": 0}
 
@@ -195,3 +199,38 @@ def check_device_status(device: torch.device | int | None = None, sync: bool = T
             f"sparsecore_b200: a bounded device-side wait timed out on {dev} (status word "
             f"0x{st.value:x}, SL_ERR_TIMEOUT): the outputs of kernels launched since the last "
             "status check are incomplete")
+
+
+def measure_ceilings(device: torch.device | None = None) -> dict:
+    """Measured FP32 FMA and shared-memory throughput of this GPU (the
+    library's probe kernels, CUDA events, best of 5 after a warm-up), for the
+    roofline fractions of the FMA- and shared-memory-bound kernels."""
+    dev = require_cuda(device)
+    n = int(lib().sl_probe_threads())
+    out = torch.empty(n, dtype=torch.float32, device=dev)
+    s = stream_ptr(dev)
+
+    def best_ms(name, iters):
+        fn = getattr(lib(), name)
+        check(fn(iters, ptr(out), s), name)
+        torch.cuda.synchronize(dev)
+        best = float("inf")
+        for _ in range(5):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            check(fn(iters, ptr(out), s), name)
+            b.record()
+            b.synchronize()
+            best = min(best, a.elapsed_time(b))
+        return best
+
+    it_f, it_s = 1 << 16, 1 << 14
+    ms_f = best_ms("sl_probe_ffma", it_f)
+    ms_s = best_ms("sl_probe_smem", it_s)
+    fp32 = 16.0 * it_f * n / (ms_f * 1e-3) / 1e12
+    smem = 16.0 * it_s * n / (ms_s * 1e-3) / 1e12
+    return {"fp32_tflops": round(fp32, 2), "smem_tbs": round(smem, 2),
+            "gather_ceiling_tflops": round(smem / 4.0 * 2.0, 2),
+            "how": "library probe kernels (sl_probe_ffma: 8 independent FMA chains per thread; "
+                   "sl_probe_smem: conflict-free 128-bit shared loads), 64 warps per SM, "
+                   "CUDA events, best of 5; gather ceiling = 4 B of shared/L1 operand per FMA"}

@@ -32,9 +32,9 @@ inline bool aligned16(const void* p) {
 int check_csr(const sl_csr* W, const char* fn);
 // Grid size for warp-per-row kernels of 256 threads (8 warps per CTA).
 int row_grid(int64_t M);
-// N = 1 forward with per-lane bulk-copied row windows (spmv_bulk.cu);
+// N = 1 forward, warp-specialised row windows (spmv_ws.cu);
 // -1 when it does not apply.
-int launch_spmv_bulk(const sl_csr* W, const float* X, int64_t K, float* Y, cudaStream_t s);
+int launch_spmv_ws(const sl_csr* W, const float* X, int64_t K, float* Y, cudaStream_t s);
 // N = 32 forward / SDDMM with X rows staged by cp.async (gather32.cu); -1
 // when they do not apply.
 int launch_gather32_fwd(const sl_csr* W, const float* X, float* Y, cudaStream_t s);

@@ -254,9 +254,6 @@ constexpr int kTJ = 32;                   // columns per chunk: 128-byte rows
 constexpr int kTMaxRows = 128;
 constexpr int kTStages = 5;
 
-// Float offset of float4 `chunk` (0..7) of `row` in a 128B-swizzled tile.
-__device__ __forceinline__ int sw(int row, int chunk) { return row * kTJ + ((chunk ^ (row & 7)) << 2); }
-
 __device__ __forceinline__ int lower_bound_cols(const int32_t* __restrict__ c, int n, int key) {
     int lo = 0, hi = n;
     while (lo < hi) {

@@ -982,7 +982,7 @@ extern "C" int sl_spmm_fwd(const sl_csr* W, const float* X, int64_t K, int64_t N
     if (N == 1 && spmv_lane_enabled(W)) {
         // SPARSECORE_B200_N1=lane keeps the cp.async lane kernel (tests).
         const char* e = std::getenv("SPARSECORE_B200_N1");
-        int rc = (e != nullptr && e[0] == 'l') ? -1 : launch_spmv_bulk(W, X, K, Y, s);
+        int rc = (e != nullptr && e[0] == 'l') ? -1 : launch_spmv_ws(W, X, K, Y, s);
         if (rc < 0) rc = launch_spmv(W, X, K, Y, s);
         if (rc >= 0) return rc;
     }

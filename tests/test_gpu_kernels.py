@@ -236,8 +236,9 @@ def test_mid_n_sddmm_and_forward_vs_oracle(M, K, N, block, monkeypatch):
                                       (12000, 300, 0.9, 0.0), (7, 5, 0.3, 0.0), (4733, 1001, 0.8, 0.0),
                                       (300, 17000, 0.9, 0.2)])
 def test_spmv_lane_kernel_matches_oracle_and_warp_kernel(M, K, s, pr, monkeypatch):
-    """N = 1: forward / dX on the lane-per-row kernels (cooperatively copied
-    row windows by default, both ring depths; the per-lane cp.async variant) and the
+    """N = 1: forward / dX on the lane-per-row kernels (warp-specialised row
+    windows by default, both ring depths, X staged or through L1; the per-lane
+    cp.async variant) and the
     streaming SDDMM, against the oracle and the general kernels: ragged and
     empty rows, rows whose 4-slot groups start unaligned or run past the
     arrays' end (no padding, total capacity not a multiple of 4), K above
@@ -265,14 +266,14 @@ def test_spmv_lane_kernel_matches_oracle_and_warp_kernel(M, K, s, pr, monkeypatc
     assert bits_equal(y, O.spmm(Wo, X.numpy()))
     assert bits_equal(dx, O.spmm(WTo, dY.numpy()))
     assert bits_equal(dw, O.sddmm(Wo, dY.numpy(), X.numpy()))
-    for ws in ("2", "1", "0"):  # warp-specialised (bulk / cp.async copies), single-warp
-        monkeypatch.setenv("SPARSECORE_B200_N1_WS", ws)
+    for xs in ("1", "0"):  # X in shared memory / through L1
+        monkeypatch.setenv("SPARSECORE_B200_N1_XS", xs)
         for st in ("4", "8"):  # both ring depths
             monkeypatch.setenv("SPARSECORE_B200_N1_ST", st)
-            assert bits_equal(sl.spmm(W, X.to(d)), y), (ws, st)
-            assert bits_equal(ops._spmm_raw(WT, dY.to(d)), dx), (ws, st)
+            assert bits_equal(sl.spmm(W, X.to(d)), y), (xs, st)
+            assert bits_equal(ops._spmm_raw(WT, dY.to(d)), dx), (xs, st)
     monkeypatch.delenv("SPARSECORE_B200_N1_ST")
-    monkeypatch.delenv("SPARSECORE_B200_N1_WS")
+    monkeypatch.delenv("SPARSECORE_B200_N1_XS")
     monkeypatch.setenv("SPARSECORE_B200_N1", "lane")  # the cp.async lane kernel
     assert bits_equal(sl.spmm(W, X.to(d)), y)
     assert bits_equal(ops._spmm_raw(WT, dY.to(d)), dx)
