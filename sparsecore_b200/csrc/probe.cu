@@ -34,11 +34,17 @@ __global__ void __launch_bounds__(256) probe_smem_kernel(int64_t iters, float* o
         buf[k] = make_float4(k, k + 1, k + 2, k + 3);
     __syncthreads();
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    int idx = threadIdx.x & 1023;
+    const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(buf));
+    uint32_t off = (threadIdx.x & 1023) * 16;
     for (int64_t i = 0; i < iters; ++i) {
-        const float4 v = buf[idx];
+        float4 v;
+        // volatile: every iteration's load is issued (the addresses repeat
+        // every 4 iterations, which a compiler could otherwise hoist).
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                     : "r"(base + off));
         acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
-        idx = (idx + 256) & 1023;  // consecutive lanes, consecutive 16-byte words
+        off = (off + 4096) & 16383;  // consecutive lanes, consecutive 16-byte words
     }
     out[blockIdx.x * blockDim.x + threadIdx.x] = acc.x + acc.y + acc.z + acc.w;
 }

@@ -981,8 +981,17 @@ extern "C" int sl_spmm_fwd(const sl_csr* W, const float* X, int64_t K, int64_t N
     }
     if (N == 1 && spmv_lane_enabled(W)) {
         // SPARSECORE_B200_N1=lane keeps the cp.async lane kernel (tests).
+        // Measured on B200 (4096 and 16384 rows x 4096, 50-99%): the
+        // warp-specialised window kernel wins with long rows (with one CTA
+        // per SM from about 100 slots per row, with more rows from about
+        // 600); short rows keep the per-lane kernel, whose start-up is
+        // cheaper.  SPARSECORE_B200_N1=lane|ws forces one (tests).
         const char* e = std::getenv("SPARSECORE_B200_N1");
-        int rc = (e != nullptr && e[0] == 'l') ? -1 : launch_spmv_ws(W, X, K, Y, s);
+        const double avg = static_cast<double>(W->total_capacity) / 1.2 / static_cast<double>(W->nrows);
+        bool ws = (W->nrows + 31) / 32 <= num_sms() ? avg >= 96.0 : avg >= 600.0;
+        if (e != nullptr && e[0] == 'l') ws = false;
+        if (e != nullptr && e[0] == 'w' && e[1] == 's') ws = true;
+        int rc = ws ? launch_spmv_ws(W, X, K, Y, s) : -1;
         if (rc < 0) rc = launch_spmv(W, X, K, Y, s);
         if (rc >= 0) return rc;
     }

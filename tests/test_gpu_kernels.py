@@ -266,6 +266,7 @@ def test_spmv_lane_kernel_matches_oracle_and_warp_kernel(M, K, s, pr, monkeypatc
     assert bits_equal(y, O.spmm(Wo, X.numpy()))
     assert bits_equal(dx, O.spmm(WTo, dY.numpy()))
     assert bits_equal(dw, O.sddmm(Wo, dY.numpy(), X.numpy()))
+    monkeypatch.setenv("SPARSECORE_B200_N1", "ws")  # forced: short rows default to the lane kernel
     for xs in ("1", "0"):  # X in shared memory / through L1
         monkeypatch.setenv("SPARSECORE_B200_N1_XS", xs)
         for st in ("4", "8"):  # both ring depths
