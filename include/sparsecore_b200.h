@@ -259,6 +259,20 @@ SL_API int sl_set_regrow_draws(uint64_t* pcg_state, int32_t* has_uint32, uint32_
 SL_API int sl_transpose_f32(const float* src, int64_t rows, int64_t cols, float* dst,
                      void* stream);
 
+/* Fused AdamW over a SparseLinear's live slots (the "fused optimizer over
+ * padded values" item of the reference's sparse-training path; the reference
+ * itself runs torch's AdamW over the whole padded values tensor,
+ * sparselab/nn.py:183-184).  One pass over W's slots: padding slots (col -1)
+ * are skipped -- their value stays 0 and their moments untouched -- and each
+ * live slot gets torch.optim.AdamW's update with decoupled weight decay:
+ *   p *= 1 - lr*wd;  m = lerp(m, g, 1 - beta1);  v = beta2*v + (1-beta2)*g*g;
+ *   p -= lr / (1 - beta1^step) * m / (sqrt(v) / sqrt(1 - beta2^step) + eps).
+ * grad / exp_avg / exp_avg_sq are float[total_capacity] aligned with
+ * W->values (updated in place); step >= 1 is the step being taken. */
+SL_API int sl_adamw_live(const sl_csr* W, const float* grad, float* exp_avg, float* exp_avg_sq,
+                  float lr, float beta1, float beta2, float eps, float weight_decay,
+                  int64_t step, void* stream);
+
 /* ── Data-parallel packing of live gradient slots ────────────────────────
  * packed_offsets[nrows] = exclusive scan of row_nnz.  pack copies the live
  * slots of src[total_capacity] into dst[nnz]; unpack scatters back into

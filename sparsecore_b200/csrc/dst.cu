@@ -19,6 +19,8 @@
 //    RigL - grown columns = the n_grow non-survivors of largest |G[i,:]|
 //           (router.py:699-721, np.argpartition).  When that set is not
 //           unique (ties at the cut) the row is flagged for the host.
+#include <cmath>
+
 #include "common.cuh"
 
 namespace slb {
@@ -408,3 +410,60 @@ int sl_dst_apply_cols(const sl_csr* W, const float* thr_dev, const int32_t* forc
 }
 
 }  // extern "C"
+
+// ── Fused AdamW over live slots ─────────────────────────────────────────
+// One pass over a SparseLinear's padded values: slots whose column is -1
+// (padding) are skipped, so their value stays exactly 0 and their moments
+// are not touched; live slots get torch's decoupled-weight-decay AdamW
+// update (param *= 1 - lr*wd; m = lerp(m, g, 1-b1); v = b2*v + (1-b2)*g*g;
+// param -= lr/bc1 * m / (sqrt(v)/sqrt(bc2) + eps)).  State is per slot, as
+// with a torch optimizer on the aliased values tensor: a topology rewrite
+// moves weights between slots and the moments stay with the slot.
+namespace slb {
+namespace {
+__global__ void __launch_bounds__(256)
+adamw_live_kernel(int64_t cap, const int32_t* __restrict__ cols, float* __restrict__ p,
+                  const float* __restrict__ g, float* __restrict__ m, float* __restrict__ v,
+                  float decay, float one_minus_b1, float b2, float one_minus_b2, float eps,
+                  float step_size, float bc2_sqrt) {
+    for (int64_t s = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; s < cap;
+         s += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        if (__ldg(cols + s) < 0) continue;
+        const float gs = __ldg(g + s);
+        float ps = p[s] * decay;
+        const float ms = m[s] + one_minus_b1 * (gs - m[s]);
+        const float vs = v[s] * b2 + one_minus_b2 * gs * gs;
+        const float denom = sqrtf(vs) / bc2_sqrt + eps;
+        ps = ps - step_size * (ms / denom);
+        p[s] = ps;
+        m[s] = ms;
+        v[s] = vs;
+    }
+}
+}  // namespace
+}  // namespace slb
+
+extern "C" int sl_adamw_live(const sl_csr* W, const float* grad, float* exp_avg,
+                             float* exp_avg_sq, float lr, float beta1, float beta2, float eps,
+                             float weight_decay, int64_t step, void* stream) {
+    if (int rc = check_csr(W, "sl_adamw_live")) return rc;
+    SL_REQUIRE(step >= 1, "sl_adamw_live", "step must be >= 1");
+    SL_REQUIRE(lr >= 0.0f && eps >= 0.0f && beta1 >= 0.0f && beta1 < 1.0f && beta2 >= 0.0f &&
+                   beta2 < 1.0f,
+               "sl_adamw_live", "invalid hyper-parameters");
+    if (W->total_capacity == 0) return SL_OK;
+    SL_REQUIRE(grad != nullptr && exp_avg != nullptr && exp_avg_sq != nullptr, "sl_adamw_live",
+               "NULL gradient or state");
+    const double bc1 = 1.0 - std::pow(static_cast<double>(beta1), static_cast<double>(step));
+    const double bc2 = 1.0 - std::pow(static_cast<double>(beta2), static_cast<double>(step));
+    const int64_t cap = W->total_capacity;
+    int64_t blocks = (cap + 255) / 256;
+    const int64_t max_blocks = static_cast<int64_t>(num_sms()) * 8;
+    if (blocks > max_blocks) blocks = max_blocks;
+    adamw_live_kernel<<<static_cast<unsigned>(blocks), 256, 0, as_stream(stream)>>>(
+        cap, W->col_indices, W->values, grad, exp_avg, exp_avg_sq,
+        1.0f - lr * weight_decay, 1.0f - beta1, beta2, 1.0f - beta2, eps,
+        static_cast<float>(lr / bc1), static_cast<float>(std::sqrt(bc2)));
+    SL_RETURN_IF_LAUNCH_FAILED("sl_adamw_live");
+    return SL_OK;
+}
