@@ -197,6 +197,36 @@ SL_API int sl_check_invariants(const sl_csr* W, int64_t n_slots, int64_t* report
 SL_API int sl_dense_grad(const float* dY, const float* X, int64_t M, int64_t K,
                   int64_t N, float* G, void* stream);
 
+/* RigL grow selection without materialising G (sparselab/router.py:631-721:
+ * G = dense_grad(dY, X), survivors masked to -inf, np.argpartition of -|G|
+ * per row; the streaming top-k of docs/design/rigl.md:86-93), in three
+ * calls after sl_dst_threshold / sl_dst_keep:
+ *   sl_rigl_prep: survivor bitmap uint32[M][ceil(K/32)] (|v| > thr or the
+ *     row's forced keep) and n_grow[M] = min(n_drop, K - n_keep) (0 for
+ *     empty rows);
+ *   sl_rigl_candidates: the dense-gradient GEMM (same per-element rounding
+ *     as sl_dense_grad) whose epilogue keeps, per row and 128-column tile,
+ *     the min(n_grow + 1, lmax) largest candidate keys (|G| bits + 1) and
+ *     their columns: cand_key / cand_col [M][ceil(K/128)][lmax], cand_cnt
+ *     [M][ceil(K/128)]; lmax in [1, 128] must be >= n_grow + 1 for every
+ *     row or 128.  row_flag[M] must be zero on entry; bit 0 is set for rows
+ *     with a NaN candidate;
+ *   sl_rigl_merge: per row the n_grow largest keys become grow_cols at
+ *     grow_offsets[row] (exclusive scan of n_grow); rows where the next key
+ *     ties the cut, or with a NaN, get row_flag = 1 and row_mask = 0 (the
+ *     caller resolves them with the reference's argpartition on G rows it
+ *     recomputes); other live rows get row_mask = 1 for sl_dst_apply_cols. */
+SL_API int sl_rigl_prep(const sl_csr* W, const float* thr_dev, const int32_t* force_idx,
+                 uint32_t* survivor_bits, int32_t* n_grow, void* stream);
+SL_API int sl_rigl_candidates(const float* dY, const float* X, int64_t M, int64_t K, int64_t N,
+                       const uint32_t* survivor_bits, const int32_t* n_grow, int64_t lmax,
+                       uint32_t* cand_key, int32_t* cand_col, int32_t* cand_cnt,
+                       int32_t* row_flag, void* stream);
+SL_API int sl_rigl_merge(int64_t M, int64_t K, int64_t lmax, const uint32_t* cand_key,
+                  const int32_t* cand_col, const int32_t* cand_cnt, const int32_t* n_grow,
+                  const int32_t* grow_offsets, const int32_t* row_nnz, int32_t* row_flag,
+                  int32_t* row_mask, int32_t* grow_cols, void* stream);
+
 /* ── Dynamic-sparsity prune / regrow (sparselab/router.py) ───────────────
  * sl_dst_threshold: k-th smallest |value| (1-based k) over all live slots,
  *   exact (router.py:395-412, np.partition).  Writes the float to *thr_dev.

@@ -62,6 +62,9 @@ SIGNATURES: dict[str, tuple] = {
     "sl_to_dense": (I32, [P, P, P]),
     "sl_check_invariants": (I32, [P, I64, P, P]),
     "sl_dense_grad": (I32, [P, P, I64, I64, I64, P, P]),
+    "sl_rigl_prep": (I32, [P, P, P, P, P, P]),
+    "sl_rigl_candidates": (I32, [P, P, I64, I64, I64, P, P, I64, P, P, P, P, P]),
+    "sl_rigl_merge": (I32, [I64, I64, I64, P, P, P, P, P, P, P, P, P, P]),
     "sl_dst_scratch_bytes": (I64, []),
     "sl_dst_max_ncols": (I64, []),
     "sl_dst_threshold": (I32, [P, I64, P, P, P]),
@@ -140,7 +143,7 @@ KERNELS_PER_CALL = {
     "sl_spmm_fwd": 1, "sl_sddmm_dw": 1, "sl_transpose_count": 3, "sl_transpose_fill": 2,
     "sl_transpose_with_perm_noalloc": 5,
     "sl_values_gather": 1, "sl_dense_count": 2, "sl_dense_fill": 1, "sl_capacity_scan": 1,
-    "sl_to_dense": 1, "sl_check_invariants": 2, "sl_dense_grad": 1, "sl_dst_threshold": 9,
+    "sl_to_dense": 1, "sl_check_invariants": 2, "sl_dense_grad": 1, "sl_rigl_prep": 1, "sl_rigl_candidates": 1, "sl_rigl_merge": 1, "sl_dst_threshold": 9,
     "sl_dst_keep": 1, "sl_dst_apply_random": 1, "sl_dst_apply_topk": 1, "sl_dst_apply_cols": 1,
     "sl_pack_live": 1, "sl_unpack_live": 1, "sl_adamw_live": 1, "sl_exclusive_scan": 1,
     "sl_set_regrow_draws": 0,  # host only

@@ -104,10 +104,26 @@ dense_grad_kernel(const float* __restrict__ A, const float* __restrict__ B, int 
 // results are bit-identical to the 64x64 kernel's.
 constexpr int BB = 128, BJ2 = 8;
 
-template <bool VEC4>
+// Epilogue of the fused RigL path (TOPK): instead of storing the tile, the
+// CTA turns it into per-row grow candidates.  key = |G| bits + 1 for
+// candidate columns (not survivors, inside K), 0 otherwise; each row keeps
+// its L = min(n_grow + 1, Lmax) largest keys of the tile's 128 columns (ties
+// by lowest column).  A NaN candidate flags the row (the host resolves it).
+struct TopkArgs {
+    const uint32_t* bits;   // survivors: [M][ceil(K/32)] bitmap
+    const int32_t* n_grow;  // [M]
+    int lmax;
+    int tiles;              // ceil(K / 128)
+    uint32_t* cand_key;     // [M][tiles][lmax]
+    int32_t* cand_col;      // [M][tiles][lmax]
+    int32_t* cand_cnt;      // [M][tiles]
+    int32_t* row_flag;      // [M], bit 0 = resolve on the host
+};
+
+template <bool VEC4, bool TOPK>
 __global__ void __launch_bounds__(kGThreads)
 dense_grad128_kernel(const float* __restrict__ A, const float* __restrict__ B, int M, int K,
-                     int64_t N, float* __restrict__ G) {
+                     int64_t N, float* __restrict__ G, TopkArgs ta) {
     __shared__ __align__(16) float As[2][BJ2][BB + 4];
     __shared__ __align__(16) float Bs[2][BJ2][BB + 4];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
@@ -180,14 +196,164 @@ dense_grad128_kernel(const float* __restrict__ A, const float* __restrict__ B, i
         }
         buf ^= 1;
     }
+    if constexpr (!TOPK) {
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-        const int m = m0 + (r < 4 ? ty * 4 + r : 64 + ty * 4 + r - 4);
-        if (m >= M) continue;
+        for (int r = 0; r < 8; ++r) {
+            const int m = m0 + (r < 4 ? ty * 4 + r : 64 + ty * 4 + r - 4);
+            if (m >= M) continue;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const int k = k0 + (c < 4 ? tx * 4 + c : 64 + tx * 4 + c - 4);
-            if (k < K) G[static_cast<int64_t>(m) * K + k] = acc[r][c];
+            for (int c = 0; c < 8; ++c) {
+                const int k = k0 + (c < 4 ? tx * 4 + c : 64 + tx * 4 + c - 4);
+                if (k < K) G[static_cast<int64_t>(m) * K + k] = acc[r][c];
+            }
+        }
+    } else {
+        extern __shared__ uint32_t keys[];  // [128][129]
+        const int KW = (K + 31) >> 5;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            const int lr2 = r < 4 ? ty * 4 + r : 64 + ty * 4 + r - 4;
+            const int m = m0 + lr2;
+            bool nan_row = false;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const int lc = c < 4 ? tx * 4 + c : 64 + tx * 4 + c - 4;
+                const int k = k0 + lc;
+                uint32_t key = 0;
+                if (m < M && k < K &&
+                    !((__ldg(ta.bits + static_cast<int64_t>(m) * KW + (k >> 5)) >> (k & 31)) & 1u)) {
+                    const uint32_t a = __float_as_uint(acc[r][c]) & 0x7fffffffu;
+                    nan_row |= a > 0x7f800000u;
+                    key = a + 1u;
+                }
+                keys[lr2 * 129 + lc] = key;
+            }
+            if (nan_row) atomicOr(ta.row_flag + m, 1);
+        }
+        __syncthreads();
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        const int tile = blockIdx.x;
+        for (int lr2 = warp; lr2 < BB; lr2 += kGThreads / 32) {
+            const int m = m0 + lr2;
+            if (m >= M) break;
+            const int L = min(__ldg(ta.n_grow + m) + 1, ta.lmax);
+            uint32_t kv[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) kv[q] = keys[lr2 * 129 + lane + 32 * q];
+            const int64_t base = (static_cast<int64_t>(m) * ta.tiles + tile) * ta.lmax;
+            int cnt = 0;
+            for (; cnt < L; ++cnt) {
+                // largest key of the row; ties -> lowest column
+                uint32_t best = kv[0];
+                int bq = 0;
+#pragma unroll
+                for (int q = 1; q < 4; ++q)
+                    if (kv[q] > best) { best = kv[q]; bq = q; }
+                int bcol = lane + 32 * bq;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const uint32_t ob = __shfl_xor_sync(0xffffffffu, best, o);
+                    const int oc = __shfl_xor_sync(0xffffffffu, bcol, o);
+                    if (ob > best || (ob == best && oc < bcol)) { best = ob; bcol = oc; }
+                }
+                if (best == 0u) break;  // no candidate left in this tile
+                if (lane == 0) {
+                    ta.cand_key[base + cnt] = best;
+                    ta.cand_col[base + cnt] = k0 + bcol;
+                }
+                if (lane == (bcol & 31)) kv[bcol >> 5] = 0u;
+            }
+            if (lane == 0) ta.cand_cnt[static_cast<int64_t>(m) * ta.tiles + tile] = cnt;
+        }
+    }
+}
+
+// Survivor bitmap and grow count per row for the fused RigL path: a slot
+// survives when |v| > thr or it is the row's forced keep (the same rule as
+// the rewrite kernel); n_grow = min(n_drop, K - n_keep), 0 for empty rows.
+__global__ void __launch_bounds__(256)
+rigl_prep_kernel(int M, int K, const int32_t* __restrict__ row_start,
+                 const int32_t* __restrict__ row_nnz, const int32_t* __restrict__ cols,
+                 const float* __restrict__ vals, const float* __restrict__ thr_dev,
+                 const int32_t* __restrict__ force_idx, uint32_t* __restrict__ bits,
+                 int32_t* __restrict__ n_grow) {
+    const int lane = threadIdx.x & 31;
+    const int KW = (K + 31) >> 5;
+    const float thr = *thr_dev;
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < M; row += warps) {
+        uint32_t* br = bits + static_cast<int64_t>(row) * KW;
+        for (int w = lane; w < KW; w += 32) br[w] = 0u;
+        __syncwarp();
+        const int rs = row_start[row], nn = row_nnz[row], fidx = force_idx[row];
+        int keep = 0;
+        for (int s = lane; s < nn; s += 32) {
+            if (fabsf(vals[rs + s]) > thr || s == fidx) {
+                const int c = cols[rs + s];
+                atomicOr(br + (c >> 5), 1u << (c & 31));
+                ++keep;
+            }
+        }
+        keep = warp_sum(keep);
+        if (lane == 0) n_grow[row] = nn > 0 ? min(nn - keep, K - keep) : 0;
+    }
+}
+
+// Merge the tiles' candidates of each row: the n_grow largest keys are the
+// grown columns, unless the (n_grow+1)-th key equals the n_grow-th (ties
+// straddle the cut: numpy's argpartition decides, so the row goes to the
+// host) or a NaN was seen.  row_mask = 1 for rows rewritten on the device.
+__global__ void __launch_bounds__(256)
+rigl_merge_kernel(int M, int tiles, int lmax, const uint32_t* __restrict__ cand_key,
+                  const int32_t* __restrict__ cand_col, const int32_t* __restrict__ cand_cnt,
+                  const int32_t* __restrict__ n_grow, const int32_t* __restrict__ grow_off,
+                  const int32_t* __restrict__ row_nnz, int32_t* __restrict__ row_flag,
+                  int32_t* __restrict__ row_mask, int32_t* __restrict__ grow_cols) {
+    const int lane = threadIdx.x & 31;
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < M; row += warps) {
+        const int ng = n_grow[row];
+        int flag = row_flag[row];
+        if (row_nnz[row] == 0) {
+            if (lane == 0) row_mask[row] = 0;
+            continue;
+        }
+        const int64_t cbase = static_cast<int64_t>(row) * tiles * lmax;
+        const int ncand = tiles * lmax;
+        uint32_t prev = 0;
+        int taken = 0;
+        // Selection rounds over the row's candidates (ng + 1 of them at most);
+        // consumed ones are skipped through their key drop below `prev`.
+        for (int t = 0; t <= ng && !flag; ++t) {
+            uint32_t best = 0u;
+            int bcol = INT_MAX;
+            for (int e = lane; e < ncand; e += 32) {
+                const int tl = e / lmax, q = e % lmax;
+                if (q >= cand_cnt[static_cast<int64_t>(row) * tiles + tl]) continue;
+                const uint32_t k = cand_key[cbase + e];
+                const int c = cand_col[cbase + e];
+                // strictly after the previous pick in (key desc, col asc) order
+                const bool after = t == 0 || k < prev || (k == prev && c > taken);
+                if (after && (k > best || (k == best && c < bcol))) { best = k; bcol = c; }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const uint32_t ob = __shfl_xor_sync(0xffffffffu, best, o);
+                const int oc = __shfl_xor_sync(0xffffffffu, bcol, o);
+                if (ob > best || (ob == best && oc < bcol)) { best = ob; bcol = oc; }
+            }
+            if (t < ng) {
+                if (best == 0u) { flag = 1; break; }  // fewer candidates than n_grow
+                if (lane == 0) grow_cols[grow_off[row] + t] = bcol;
+            } else if (best != 0u && best == prev) {
+                flag = 1;  // the (n_grow+1)-th key ties the n_grow-th
+            }
+            prev = best;
+            taken = bcol;
+        }
+        if (lane == 0) {
+            row_flag[row] = flag;
+            row_mask[row] = flag ? 0 : 1;
         }
     }
 }
@@ -216,11 +382,11 @@ extern "C" int sl_dense_grad(const float* dY, const float* X, int64_t M, int64_t
     if (big) {
         const dim3 g2(static_cast<unsigned>((K + BB - 1) / BB), static_cast<unsigned>((M + BB - 1) / BB));
         if (vec4)
-            dense_grad128_kernel<true><<<g2, kGThreads, 0, s>>>(dY, X, static_cast<int>(M),
-                                                                static_cast<int>(K), N, G);
+            dense_grad128_kernel<true, false><<<g2, kGThreads, 0, s>>>(dY, X, static_cast<int>(M),
+                                                                       static_cast<int>(K), N, G, TopkArgs{});
         else
-            dense_grad128_kernel<false><<<g2, kGThreads, 0, s>>>(dY, X, static_cast<int>(M),
-                                                                 static_cast<int>(K), N, G);
+            dense_grad128_kernel<false, false><<<g2, kGThreads, 0, s>>>(dY, X, static_cast<int>(M),
+                                                                        static_cast<int>(K), N, G, TopkArgs{});
         SL_RETURN_IF_LAUNCH_FAILED("sl_dense_grad");
         return SL_OK;
     }
@@ -232,5 +398,64 @@ extern "C" int sl_dense_grad(const float* dY, const float* X, int64_t M, int64_t
         dense_grad_kernel<false><<<grid, kGThreads, 0, s>>>(dY, X, static_cast<int>(M),
                                                             static_cast<int>(K), N, G);
     SL_RETURN_IF_LAUNCH_FAILED("sl_dense_grad");
+    return SL_OK;
+}
+
+extern "C" int sl_rigl_prep(const sl_csr* W, const float* thr_dev, const int32_t* force_idx,
+                            uint32_t* survivor_bits, int32_t* n_grow, void* stream) {
+    if (int rc = check_csr(W, "sl_rigl_prep")) return rc;
+    if (W->nrows == 0) return SL_OK;
+    SL_REQUIRE(thr_dev != nullptr && force_idx != nullptr && survivor_bits != nullptr &&
+                   n_grow != nullptr,
+               "sl_rigl_prep", "NULL argument");
+    if (W->ncols > INT_MAX - 32) return fail(SL_ERR_UNSUPPORTED, "sl_rigl_prep: ncols beyond int32");
+    rigl_prep_kernel<<<row_grid(W->nrows), 256, 0, as_stream(stream)>>>(
+        static_cast<int>(W->nrows), static_cast<int>(W->ncols), W->row_start, W->row_nnz,
+        W->col_indices, W->values, thr_dev, force_idx, survivor_bits, n_grow);
+    SL_RETURN_IF_LAUNCH_FAILED("sl_rigl_prep");
+    return SL_OK;
+}
+
+extern "C" int sl_rigl_candidates(const float* dY, const float* X, int64_t M, int64_t K, int64_t N,
+                                  const uint32_t* survivor_bits, const int32_t* n_grow,
+                                  int64_t lmax, uint32_t* cand_key, int32_t* cand_col,
+                                  int32_t* cand_cnt, int32_t* row_flag, void* stream) {
+    const char* fn = "sl_rigl_candidates";
+    if (M < 0 || K < 0 || N < 1) return fail(SL_ERR_INVALID, std::string(fn) + ": bad shape");
+    if (M > INT_MAX || K > INT_MAX - 128) return fail(SL_ERR_UNSUPPORTED, std::string(fn) + ": shape beyond int32");
+    if (lmax < 1 || lmax > 128) return fail(SL_ERR_INVALID, std::string(fn) + ": lmax must be in [1, 128]");
+    if (M == 0 || K == 0) return SL_OK;
+    SL_REQUIRE(dY && X && survivor_bits && n_grow && cand_key && cand_col && cand_cnt && row_flag, fn,
+               "NULL argument");
+    const size_t smem = static_cast<size_t>(BB) * 129 * 4;
+    const bool vec4 = (N % 4 == 0) && aligned16(dY) && aligned16(X);
+    auto kern = vec4 ? dense_grad128_kernel<true, true> : dense_grad128_kernel<false, true>;
+    if (int rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  static_cast<int>(smem)), fn))
+        return rc;
+    TopkArgs ta{survivor_bits, n_grow, static_cast<int>(lmax), static_cast<int>((K + BB - 1) / BB),
+                cand_key, cand_col, cand_cnt, row_flag};
+    const dim3 g2(static_cast<unsigned>((K + BB - 1) / BB), static_cast<unsigned>((M + BB - 1) / BB));
+    kern<<<g2, kGThreads, smem, as_stream(stream)>>>(dY, X, static_cast<int>(M), static_cast<int>(K), N,
+                                                     nullptr, ta);
+    SL_RETURN_IF_LAUNCH_FAILED(fn);
+    return SL_OK;
+}
+
+extern "C" int sl_rigl_merge(int64_t M, int64_t K, int64_t lmax, const uint32_t* cand_key,
+                             const int32_t* cand_col, const int32_t* cand_cnt,
+                             const int32_t* n_grow, const int32_t* grow_offsets,
+                             const int32_t* row_nnz, int32_t* row_flag, int32_t* row_mask,
+                             int32_t* grow_cols, void* stream) {
+    const char* fn = "sl_rigl_merge";
+    if (M < 0 || K < 1 || lmax < 1 || lmax > 128) return fail(SL_ERR_INVALID, std::string(fn) + ": bad arguments");
+    if (M == 0) return SL_OK;
+    SL_REQUIRE(cand_key && cand_col && cand_cnt && n_grow && grow_offsets && row_nnz && row_flag &&
+                   row_mask && grow_cols,
+               fn, "NULL argument");
+    rigl_merge_kernel<<<row_grid(M), 256, 0, as_stream(stream)>>>(
+        static_cast<int>(M), static_cast<int>((K + BB - 1) / BB), static_cast<int>(lmax), cand_key,
+        cand_col, cand_cnt, n_grow, grow_offsets, row_nnz, row_flag, row_mask, grow_cols);
+    SL_RETURN_IF_LAUNCH_FAILED(fn);
     return SL_OK;
 }

@@ -239,13 +239,22 @@ class RigL(DynamicSparsityAlgorithm):
     ``capture="every_step"`` (default, the reference's behaviour) clones each
     layer's input and output gradient on every step; ``capture="update_step"``
     clones them only on steps whose ``step()`` will trigger an update.
+
+    ``fused_grow=True`` (default) picks the grown columns without
+    materialising the M x K dense gradient: the gradient GEMM keeps each
+    row's best candidates per 128-column tile and a merge kernel selects the
+    row's top n_grow (``sl_rigl_prep / sl_rigl_candidates / sl_rigl_merge``).
+    Rows whose cut is a tie (or holds a NaN) are resolved exactly as before,
+    with numpy's argpartition on their recomputed gradient rows.  The
+    topology is identical to the materialised path (``fused_grow=False``).
     """
 
     def __init__(self, sparsity: float, drop_fraction: float = 0.3, update_freq: int = 100,
-                 seed: int | None = None, capture: str = "every_step"):
+                 seed: int | None = None, capture: str = "every_step", fused_grow: bool = True):
         super().__init__(sparsity=sparsity, drop_fraction=drop_fraction, update_freq=update_freq)
         if capture not in ("every_step", "update_step"):
             raise ValueError(f"capture must be 'every_step' or 'update_step', got {capture!r}")
+        self.fused_grow = bool(fused_grow)
         self._rng = np.random.default_rng(seed)
         self._captured: dict[int, dict] = {}
         self._hook_handles: list = []
@@ -293,7 +302,23 @@ class RigL(DynamicSparsityAlgorithm):
         dY_flat = cap["dY"].reshape(-1, layer.out_features)
         return dense_grad(dY_flat.t().contiguous(), X_flat.t().contiguous())
 
+    def _operands(self, layer):
+        """(dY^T [M, N], X^T [K, N]) of the captured step, or None."""
+        cap = self._captured.get(id(layer))
+        if cap is None or "X" not in cap or "dY" not in cap:
+            return None
+        X_flat = cap["X"].reshape(-1, layer.in_features)
+        dY_flat = cap["dY"].reshape(-1, layer.out_features)
+        return (dY_flat.t().to(torch.float32).contiguous(), X_flat.t().to(torch.float32).contiguous())
+
     def _update_layer(self, layer, rng, G: torch.Tensor | None = None) -> None:
+        if G is None and self.fused_grow:
+            ops = self._operands(layer)
+            if ops is None:
+                return
+            if ops[0].shape[1] > 0 and layer._csr.nnz > 0:
+                self._update_layer_fused(layer, *ops)
+                return
         if G is None:
             G = self.dense_grad(layer)
             if G is None:
@@ -314,6 +339,50 @@ class RigL(DynamicSparsityAlgorithm):
         flagged = np.nonzero((flags_h != 0) & (csr._rn_h > 0))[0]
         if flagged.size:
             self._resolve_on_host(csr, pr, G, flagged)
+        pr.finish()
+        self._captured.pop(id(layer), None)
+
+    def _update_layer_fused(self, layer, dYt: torch.Tensor, Xt: torch.Tensor) -> None:
+        """Prune as usual, then grow from per-tile gradient candidates (the
+        M x K gradient is never stored); tie / NaN rows fall back to the
+        reference's argpartition on their recomputed gradient rows."""
+        csr = layer._csr
+        _check_cols(csr)
+        dev, s = csr.device, csr._stream()
+        M, K = csr.nrows, csr.ncols
+        dYt = dYt.to(dev)
+        Xt = Xt.to(dev)
+        Nn = dYt.shape[1]
+        pr = _Prune(csr, self.drop_fraction)
+        bits = torch.empty(M, (K + 31) // 32, dtype=torch.int32, device=dev)
+        n_grow = torch.empty(M, dtype=torch.int32, device=dev)
+        N.call("sl_rigl_prep", csr._abi_ref(), N.ptr(pr.thr), N.ptr(pr.force), N.ptr(bits),
+               N.ptr(n_grow), s)
+        lmax = int(min(int(csr._rn_h.max()) + 1, 128))
+        tiles = (K + 127) // 128
+        cand_key = torch.empty(M * tiles * lmax, dtype=torch.int32, device=dev)
+        cand_col = torch.empty(M * tiles * lmax, dtype=torch.int32, device=dev)
+        cand_cnt = torch.empty(M * tiles, dtype=torch.int32, device=dev)
+        flags = torch.zeros(M, dtype=torch.int32, device=dev)
+        N.call("sl_rigl_candidates", N.ptr(dYt), N.ptr(Xt), M, K, Nn, N.ptr(bits), N.ptr(n_grow),
+               lmax, N.ptr(cand_key), N.ptr(cand_col), N.ptr(cand_cnt), N.ptr(flags), s)
+        off = torch.zeros(M + 1, dtype=torch.int32, device=dev)
+        total = torch.empty(1, dtype=torch.int64, device=dev)
+        N.call("sl_exclusive_scan", N.ptr(n_grow), M, N.ptr(off), N.ptr(total), s)
+        off[M:].copy_(total)  # grow lists of row i: [off[i], off[i + 1])
+        grow = torch.empty(max(csr.nnz, 1), dtype=torch.int32, device=dev)  # >= sum(n_grow)
+        mask = torch.empty(M, dtype=torch.int32, device=dev)
+        N.call("sl_rigl_merge", M, K, lmax, N.ptr(cand_key), N.ptr(cand_col), N.ptr(cand_cnt),
+               N.ptr(n_grow), N.ptr(off), N.ptr(csr.row_nnz), N.ptr(flags), N.ptr(mask),
+               N.ptr(grow), s)
+        N.call("sl_dst_apply_cols", csr._abi_ref(), N.ptr(pr.thr), N.ptr(pr.force), N.ptr(mask),
+               N.ptr(off), N.ptr(grow), s)
+        flags_h = flags.cpu().numpy()
+        flagged = np.nonzero((flags_h != 0) & (csr._rn_h > 0))[0]
+        if flagged.size:
+            idx = torch.from_numpy(flagged.astype(np.int64)).to(dev)
+            G_rows = dense_grad(dYt.index_select(0, idx), Xt)
+            self._resolve_on_host(csr, pr, _RowsOf(G_rows, flagged), flagged)
         pr.finish()
         self._captured.pop(id(layer), None)
 
@@ -352,6 +421,17 @@ class RigL(DynamicSparsityAlgorithm):
         t = [torch.from_numpy(a).to(dev) for a in (mask, off, cols)]
         N.call("sl_dst_apply_cols", csr._abi_ref(), N.ptr(pr.thr), N.ptr(pr.force),
                                           N.ptr(t[0]), N.ptr(t[1]), N.ptr(t[2]), csr._stream())
+
+
+class _RowsOf:
+    """G[i] for the rows computed (a subset of the layer's rows)."""
+
+    def __init__(self, G_rows: torch.Tensor, rows):
+        self.G = G_rows
+        self.pos = {int(r): k for k, r in enumerate(rows)}
+
+    def __getitem__(self, i):
+        return self.G[self.pos[int(i)]]
 
 
 def dense_grad(dY: torch.Tensor, X: torch.Tensor) -> torch.Tensor:

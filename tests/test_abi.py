@@ -61,3 +61,22 @@ def test_product_never_imports_oracle():
             if f.endswith(".py"):
                 src = open(os.path.join(root, f)).read()
                 assert "oracle" not in src.replace("oracle-free", ""), f
+
+
+def test_sparselab_import_surface():
+    """The reference's import paths resolve to this implementation."""
+    import sparselab
+    import sparselab.layout
+    import sparselab.nn
+    import sparselab.ops
+    import sparselab.router
+    from sparselab.ops import _SpMMFunction, _cached_transpose, _clear_transpose_cache, spmm  # noqa: F401
+    from sparselab.router import SET, RigL, Static  # noqa: F401
+
+    import sparsecore_b200
+
+    assert sparselab.PaddedCSR is sparsecore_b200.PaddedCSR
+    assert sparselab.SparseLinear is sparsecore_b200.SparseLinear
+    assert sparselab.spmm is sparsecore_b200.spmm
+    assert sparselab.router.RigL is sparsecore_b200.RigL
+    assert sparselab.layout.transpose_with_perm is sparsecore_b200.transpose_with_perm

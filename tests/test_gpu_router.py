@@ -192,3 +192,54 @@ def test_mlp_set_trajectory_matches_reference(golden):
     same1 = sha(host(model[0]._csr.col_indices)) == m["sha_cols_fc1"]
     same2 = sha(host(model[2]._csr.col_indices)) == m["sha_cols_fc2"]
     print("mlp max|dloss|", float(np.max(np.abs(got - ref))), "topology identical:", same1, same2)
+
+
+@pytest.mark.parametrize("idx", range(5))
+def test_rigl_fused_grow_matches_reference(golden, idx):
+    """The fused grow path (gradient GEMM with per-tile candidates, merge,
+    no M x K buffer) on the reference's golden RigL cases: captured operands
+    X = I, dY = G^T make the in-order dense gradient equal G exactly, so the
+    topology must equal the reference's (ties and zero gradients included:
+    those rows go to the host argpartition)."""
+    import sparsecore_b200 as sl
+
+    fin, fout, s, df, kind = golden.meta["rigl_cases"][idx]
+    p = f"rigl{idx}_"
+    W = csr_from_golden(golden, p + "in_")
+    algo = sl.RigL(sparsity=s, drop_fraction=df, update_freq=1, seed=0)
+    assert algo.fused_grow
+    layer = types.SimpleNamespace(_csr=W, in_features=fin, out_features=fout)
+    G = torch.from_numpy(golden[p + "G"])
+    algo._captured[id(layer)] = {"X": torch.eye(fin).to(dev()), "dY": G.t().contiguous().to(dev())}
+    algo._update_layer(layer, algo._rng)
+    assert csr_matches(W, golden, p + "out_")
+    assert W.topology_version == int(golden[p + "version"][0])
+    W.assert_invariants()
+
+
+@pytest.mark.parametrize("M,K,s,zero_rows", [(300, 700, 0.9, False), (1536, 384, 0.9, True),
+                                             (200, 1100, 0.5, False)])
+def test_rigl_fused_grow_equals_materialised_path(M, K, s, zero_rows):
+    """Fused and materialised grow paths on random layers (several 128-column
+    tiles, ragged edges, long rows up to the 128-candidate cap), with rows of
+    all-zero gradient (every candidate ties: host path) mixed in."""
+    import sparsecore_b200 as sl
+
+    out = []
+    for fused in (True, False):
+        g = torch.Generator().manual_seed(M + K)
+        mask = torch.rand(M, K, generator=g) >= s
+        W = sl.PaddedCSR.from_dense((torch.randn(M, K, generator=g) * mask).to(dev()))
+        X = torch.randn(64, K, generator=g)
+        dY = torch.randn(64, M, generator=g)
+        if zero_rows:
+            dY[:, ::7] = 0.0
+        algo = sl.RigL(sparsity=s, drop_fraction=0.3, update_freq=1, seed=0, fused_grow=fused)
+        layer = types.SimpleNamespace(_csr=W, in_features=K, out_features=M)
+        algo._captured[id(layer)] = {"X": X.to(dev()), "dY": dY.to(dev())}
+        algo._update_layer(layer, algo._rng)
+        W.assert_invariants()
+        out.append((host(W.col_indices), host(W.row_nnz), host(W.values), W.topology_version))
+    (a, b) = out
+    assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+    assert bits_equal(a[2], b[2]) and a[3] == b[3]
