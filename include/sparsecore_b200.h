@@ -205,12 +205,13 @@ SL_API int sl_dense_grad(const float* dY, const float* X, int64_t M, int64_t K,
  *     row's forced keep) and n_grow[M] = min(n_drop, K - n_keep) (0 for
  *     empty rows);
  *   sl_rigl_candidates: the dense-gradient GEMM (same per-element rounding
- *     as sl_dense_grad) whose epilogue keeps, per row and 128-column tile,
- *     the min(n_grow + 1, lmax) largest candidate keys (|G| bits + 1) and
- *     their columns: cand_key / cand_col [M][ceil(K/128)][lmax], cand_cnt
- *     [M][ceil(K/128)]; lmax in [1, 128] must be >= n_grow + 1 for every
- *     row or 128.  row_flag[M] must be zero on entry; bit 0 is set for rows
- *     with a NaN candidate;
+ *     as sl_dense_grad) whose epilogue keeps, per row and tile of T =
+ *     tile_cols columns (64 or 128; sl_rigl_tile_cols gives the GEMM's
+ *     preferred tiling), the min(n_grow + 1, lmax) largest candidate keys
+ *     (|G| bits + 1) and their columns: cand_key / cand_col
+ *     [M][ceil(K/T)][lmax], cand_cnt [M][ceil(K/T)]; lmax in [1, 128] must
+ *     be >= n_grow + 1 for every row or >= T.  row_flag[M] must be zero on
+ *     entry; bit 0 is set for rows with a NaN candidate;
  *   sl_rigl_merge: per row the n_grow largest keys become grow_cols at
  *     grow_offsets[row] (exclusive scan of n_grow); rows where the next key
  *     ties the cut, or with a NaN, get row_flag = 1 and row_mask = 0 (the
@@ -218,11 +219,13 @@ SL_API int sl_dense_grad(const float* dY, const float* X, int64_t M, int64_t K,
  *     recomputes); other live rows get row_mask = 1 for sl_dst_apply_cols. */
 SL_API int sl_rigl_prep(const sl_csr* W, const float* thr_dev, const int32_t* force_idx,
                  uint32_t* survivor_bits, int32_t* n_grow, void* stream);
+SL_API int64_t sl_rigl_tile_cols(int64_t M, int64_t K);
 SL_API int sl_rigl_candidates(const float* dY, const float* X, int64_t M, int64_t K, int64_t N,
                        const uint32_t* survivor_bits, const int32_t* n_grow, int64_t lmax,
-                       uint32_t* cand_key, int32_t* cand_col, int32_t* cand_cnt,
-                       int32_t* row_flag, void* stream);
-SL_API int sl_rigl_merge(int64_t M, int64_t K, int64_t lmax, const uint32_t* cand_key,
+                       int64_t tile_cols, uint32_t* cand_key, int32_t* cand_col,
+                       int32_t* cand_cnt, int32_t* row_flag, void* stream);
+SL_API int sl_rigl_merge(int64_t M, int64_t K, int64_t lmax, int64_t tile_cols,
+                  const uint32_t* cand_key,
                   const int32_t* cand_col, const int32_t* cand_cnt, const int32_t* n_grow,
                   const int32_t* grow_offsets, const int32_t* row_nnz, int32_t* row_flag,
                   int32_t* row_mask, int32_t* grow_cols, void* stream);

@@ -63,8 +63,9 @@ SIGNATURES: dict[str, tuple] = {
     "sl_check_invariants": (I32, [P, I64, P, P]),
     "sl_dense_grad": (I32, [P, P, I64, I64, I64, P, P]),
     "sl_rigl_prep": (I32, [P, P, P, P, P, P]),
-    "sl_rigl_candidates": (I32, [P, P, I64, I64, I64, P, P, I64, P, P, P, P, P]),
-    "sl_rigl_merge": (I32, [I64, I64, I64, P, P, P, P, P, P, P, P, P, P]),
+    "sl_rigl_tile_cols": (I64, [I64, I64]),
+    "sl_rigl_candidates": (I32, [P, P, I64, I64, I64, P, P, I64, I64, P, P, P, P, P]),
+    "sl_rigl_merge": (I32, [I64, I64, I64, I64, P, P, P, P, P, P, P, P, P, P]),
     "sl_dst_scratch_bytes": (I64, []),
     "sl_dst_max_ncols": (I64, []),
     "sl_dst_threshold": (I32, [P, I64, P, P, P]),

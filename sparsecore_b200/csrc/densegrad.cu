@@ -18,10 +18,80 @@ namespace {
 
 constexpr int BM = 64, BK = 64, BJ = 16, kGThreads = 256;
 
-template <bool VEC4>
+// Epilogue of the fused RigL path (TOPK): instead of storing the tile, the
+// CTA turns it into per-row grow candidates.  key = |G| bits + 1 for
+// candidate columns (not survivors, inside K), 0 otherwise; each row keeps
+// its L = min(n_grow + 1, Lmax) largest keys of the tile's 128 columns (ties
+// by lowest column).  A NaN candidate flags the row (the host resolves it).
+struct TopkArgs {
+    const uint32_t* bits;   // survivors: [M][ceil(K/32)] bitmap
+    const int32_t* n_grow;  // [M]
+    int lmax;
+    int tiles;              // ceil(K / tile width)
+    uint32_t* cand_key;     // [M][tiles][lmax]
+    int32_t* cand_col;      // [M][tiles][lmax]
+    int32_t* cand_cnt;      // [M][tiles]
+    int32_t* row_flag;      // [M], bit 0 = resolve on the host
+};
+
+
+// Per-row candidate selection of a BT x BT tile whose keys (see TopkArgs)
+// are staged in shared memory as keys[BT][BT + 1]: one warp per row keeps
+// the row's min(n_grow + 1, lmax) largest keys (ties -> lowest column).
+template <int BT>
+__device__ __forceinline__ void topk_select_tile(const uint32_t* keys, int m0, int k0, int M,
+                                                 const TopkArgs& ta, int tile) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int Q = BT / 32;
+    for (int lr2 = warp; lr2 < BT; lr2 += kGThreads / 32) {
+        const int m = m0 + lr2;
+        if (m >= M) break;
+        const int L = min(__ldg(ta.n_grow + m) + 1, ta.lmax);
+        uint32_t kv[Q];
+#pragma unroll
+        for (int q = 0; q < Q; ++q) kv[q] = keys[lr2 * (BT + 1) + lane + 32 * q];
+        const int64_t base = (static_cast<int64_t>(m) * ta.tiles + tile) * ta.lmax;
+        int cnt = 0;
+        for (; cnt < L; ++cnt) {
+            uint32_t best = kv[0];
+            int bq = 0;
+#pragma unroll
+            for (int q = 1; q < Q; ++q)
+                if (kv[q] > best) { best = kv[q]; bq = q; }
+            int bcol = lane + 32 * bq;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const uint32_t ob = __shfl_xor_sync(0xffffffffu, best, o);
+                const int oc = __shfl_xor_sync(0xffffffffu, bcol, o);
+                if (ob > best || (ob == best && oc < bcol)) { best = ob; bcol = oc; }
+            }
+            if (best == 0u) break;  // no candidate left in this tile
+            if (lane == 0) {
+                ta.cand_key[base + cnt] = best;
+                ta.cand_col[base + cnt] = k0 + bcol;
+            }
+            if (lane == (bcol & 31)) kv[bcol >> 5] = 0u;
+        }
+        if (lane == 0) ta.cand_cnt[static_cast<int64_t>(m) * ta.tiles + tile] = cnt;
+    }
+}
+
+// Candidate key of G[m][k] (0 = not a candidate); a NaN sets *nan.
+__device__ __forceinline__ uint32_t candidate_key(const TopkArgs& ta, int M, int K, int m, int k,
+                                                  float g, bool* nan) {
+    const int KW = (K + 31) >> 5;
+    if (m >= M || k >= K || ((__ldg(ta.bits + static_cast<int64_t>(m) * KW + (k >> 5)) >> (k & 31)) & 1u))
+        return 0u;
+    const uint32_t a = __float_as_uint(g) & 0x7fffffffu;
+    *nan |= a > 0x7f800000u;
+    return a + 1u;
+}
+
+
+template <bool VEC4, bool TOPK>
 __global__ void __launch_bounds__(kGThreads)
 dense_grad_kernel(const float* __restrict__ A, const float* __restrict__ B, int M, int K,
-                  int64_t N, float* __restrict__ G) {
+                  int64_t N, float* __restrict__ G, TopkArgs ta) {
     __shared__ float As[BJ][BM + 4];
     __shared__ float Bs[BJ][BK + 4];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
@@ -82,15 +152,31 @@ dense_grad_kernel(const float* __restrict__ A, const float* __restrict__ B, int 
                 for (int c = 0; c < 4; ++c) acc[r][c] = fmaf(av[r], bv[c], acc[r][c]);
         }
     }
+    if constexpr (!TOPK) {
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-        const int m = m0 + ty * 4 + r;
-        if (m >= M) continue;
+        for (int r = 0; r < 4; ++r) {
+            const int m = m0 + ty * 4 + r;
+            if (m >= M) continue;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const int k = k0 + tx * 4 + c;
-            if (k < K) G[static_cast<int64_t>(m) * K + k] = acc[r][c];
+            for (int c = 0; c < 4; ++c) {
+                const int k = k0 + tx * 4 + c;
+                if (k < K) G[static_cast<int64_t>(m) * K + k] = acc[r][c];
+            }
         }
+    } else {
+        __shared__ uint32_t keys[BM * (BM + 1)];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int m = m0 + ty * 4 + r;
+            bool nan_row = false;
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                keys[(ty * 4 + r) * (BM + 1) + tx * 4 + c] =
+                    candidate_key(ta, M, K, m, k0 + tx * 4 + c, acc[r][c], &nan_row);
+            if (nan_row) atomicOr(ta.row_flag + m, 1);
+        }
+        __syncthreads();
+        topk_select_tile<BM>(keys, m0, k0, M, ta, blockIdx.x);
     }
 }
 
@@ -103,22 +189,6 @@ dense_grad_kernel(const float* __restrict__ A, const float* __restrict__ B, int 
 // above (rounded product + add for j < 4*floor(N/4), FMA after), so the
 // results are bit-identical to the 64x64 kernel's.
 constexpr int BB = 128, BJ2 = 8;
-
-// Epilogue of the fused RigL path (TOPK): instead of storing the tile, the
-// CTA turns it into per-row grow candidates.  key = |G| bits + 1 for
-// candidate columns (not survivors, inside K), 0 otherwise; each row keeps
-// its L = min(n_grow + 1, Lmax) largest keys of the tile's 128 columns (ties
-// by lowest column).  A NaN candidate flags the row (the host resolves it).
-struct TopkArgs {
-    const uint32_t* bits;   // survivors: [M][ceil(K/32)] bitmap
-    const int32_t* n_grow;  // [M]
-    int lmax;
-    int tiles;              // ceil(K / 128)
-    uint32_t* cand_key;     // [M][tiles][lmax]
-    int32_t* cand_col;      // [M][tiles][lmax]
-    int32_t* cand_cnt;      // [M][tiles]
-    int32_t* row_flag;      // [M], bit 0 = resolve on the host
-};
 
 template <bool VEC4, bool TOPK>
 __global__ void __launch_bounds__(kGThreads)
@@ -209,7 +279,6 @@ dense_grad128_kernel(const float* __restrict__ A, const float* __restrict__ B, i
         }
     } else {
         extern __shared__ uint32_t keys[];  // [128][129]
-        const int KW = (K + 31) >> 5;
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
             const int lr2 = r < 4 ? ty * 4 + r : 64 + ty * 4 + r - 4;
@@ -218,53 +287,12 @@ dense_grad128_kernel(const float* __restrict__ A, const float* __restrict__ B, i
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
                 const int lc = c < 4 ? tx * 4 + c : 64 + tx * 4 + c - 4;
-                const int k = k0 + lc;
-                uint32_t key = 0;
-                if (m < M && k < K &&
-                    !((__ldg(ta.bits + static_cast<int64_t>(m) * KW + (k >> 5)) >> (k & 31)) & 1u)) {
-                    const uint32_t a = __float_as_uint(acc[r][c]) & 0x7fffffffu;
-                    nan_row |= a > 0x7f800000u;
-                    key = a + 1u;
-                }
-                keys[lr2 * 129 + lc] = key;
+                keys[lr2 * 129 + lc] = candidate_key(ta, M, K, m, k0 + lc, acc[r][c], &nan_row);
             }
             if (nan_row) atomicOr(ta.row_flag + m, 1);
         }
         __syncthreads();
-        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        const int tile = blockIdx.x;
-        for (int lr2 = warp; lr2 < BB; lr2 += kGThreads / 32) {
-            const int m = m0 + lr2;
-            if (m >= M) break;
-            const int L = min(__ldg(ta.n_grow + m) + 1, ta.lmax);
-            uint32_t kv[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) kv[q] = keys[lr2 * 129 + lane + 32 * q];
-            const int64_t base = (static_cast<int64_t>(m) * ta.tiles + tile) * ta.lmax;
-            int cnt = 0;
-            for (; cnt < L; ++cnt) {
-                // largest key of the row; ties -> lowest column
-                uint32_t best = kv[0];
-                int bq = 0;
-#pragma unroll
-                for (int q = 1; q < 4; ++q)
-                    if (kv[q] > best) { best = kv[q]; bq = q; }
-                int bcol = lane + 32 * bq;
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const uint32_t ob = __shfl_xor_sync(0xffffffffu, best, o);
-                    const int oc = __shfl_xor_sync(0xffffffffu, bcol, o);
-                    if (ob > best || (ob == best && oc < bcol)) { best = ob; bcol = oc; }
-                }
-                if (best == 0u) break;  // no candidate left in this tile
-                if (lane == 0) {
-                    ta.cand_key[base + cnt] = best;
-                    ta.cand_col[base + cnt] = k0 + bcol;
-                }
-                if (lane == (bcol & 31)) kv[bcol >> 5] = 0u;
-            }
-            if (lane == 0) ta.cand_cnt[static_cast<int64_t>(m) * ta.tiles + tile] = cnt;
-        }
+        topk_select_tile<BB>(keys, m0, k0, M, ta, blockIdx.x);
     }
 }
 
@@ -392,11 +420,11 @@ extern "C" int sl_dense_grad(const float* dY, const float* X, int64_t M, int64_t
     }
     const dim3 grid(static_cast<unsigned>((K + BK - 1) / BK), static_cast<unsigned>((M + BM - 1) / BM));
     if (vec4)
-        dense_grad_kernel<true><<<grid, kGThreads, 0, s>>>(dY, X, static_cast<int>(M),
-                                                           static_cast<int>(K), N, G);
+        dense_grad_kernel<true, false><<<grid, kGThreads, 0, s>>>(dY, X, static_cast<int>(M),
+                                                                  static_cast<int>(K), N, G, TopkArgs{});
     else
-        dense_grad_kernel<false><<<grid, kGThreads, 0, s>>>(dY, X, static_cast<int>(M),
-                                                            static_cast<int>(K), N, G);
+        dense_grad_kernel<false, false><<<grid, kGThreads, 0, s>>>(dY, X, static_cast<int>(M),
+                                                                   static_cast<int>(K), N, G, TopkArgs{});
     SL_RETURN_IF_LAUNCH_FAILED("sl_dense_grad");
     return SL_OK;
 }
@@ -416,45 +444,64 @@ extern "C" int sl_rigl_prep(const sl_csr* W, const float* thr_dev, const int32_t
     return SL_OK;
 }
 
+extern "C" int64_t sl_rigl_tile_cols(int64_t M, int64_t K) {
+    // The GEMM's tiling: 128x128 where those tiles fill the GPU, else 64x64.
+    // SPARSECORE_B200_DG=64|128 forces one (tests and measurements).
+    const char* e = std::getenv("SPARSECORE_B200_DG");
+    if (e != nullptr) return e[0] == '1' ? 128 : 64;
+    const int64_t tiles128 = ((M + BB - 1) / BB) * ((K + BB - 1) / BB);
+    return tiles128 >= num_sms() ? 128 : 64;
+}
+
 extern "C" int sl_rigl_candidates(const float* dY, const float* X, int64_t M, int64_t K, int64_t N,
                                   const uint32_t* survivor_bits, const int32_t* n_grow,
-                                  int64_t lmax, uint32_t* cand_key, int32_t* cand_col,
-                                  int32_t* cand_cnt, int32_t* row_flag, void* stream) {
+                                  int64_t lmax, int64_t tile_cols, uint32_t* cand_key,
+                                  int32_t* cand_col, int32_t* cand_cnt, int32_t* row_flag,
+                                  void* stream) {
     const char* fn = "sl_rigl_candidates";
     if (M < 0 || K < 0 || N < 1) return fail(SL_ERR_INVALID, std::string(fn) + ": bad shape");
     if (M > INT_MAX || K > INT_MAX - 128) return fail(SL_ERR_UNSUPPORTED, std::string(fn) + ": shape beyond int32");
     if (lmax < 1 || lmax > 128) return fail(SL_ERR_INVALID, std::string(fn) + ": lmax must be in [1, 128]");
+    if (tile_cols != 64 && tile_cols != 128) return fail(SL_ERR_INVALID, std::string(fn) + ": tile_cols must be 64 or 128");
     if (M == 0 || K == 0) return SL_OK;
     SL_REQUIRE(dY && X && survivor_bits && n_grow && cand_key && cand_col && cand_cnt && row_flag, fn,
                "NULL argument");
-    const size_t smem = static_cast<size_t>(BB) * 129 * 4;
     const bool vec4 = (N % 4 == 0) && aligned16(dY) && aligned16(X);
-    auto kern = vec4 ? dense_grad128_kernel<true, true> : dense_grad128_kernel<false, true>;
-    if (int rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                  static_cast<int>(smem)), fn))
-        return rc;
-    TopkArgs ta{survivor_bits, n_grow, static_cast<int>(lmax), static_cast<int>((K + BB - 1) / BB),
-                cand_key, cand_col, cand_cnt, row_flag};
-    const dim3 g2(static_cast<unsigned>((K + BB - 1) / BB), static_cast<unsigned>((M + BB - 1) / BB));
-    kern<<<g2, kGThreads, smem, as_stream(stream)>>>(dY, X, static_cast<int>(M), static_cast<int>(K), N,
-                                                     nullptr, ta);
+    TopkArgs ta{survivor_bits, n_grow, static_cast<int>(lmax),
+                static_cast<int>((K + tile_cols - 1) / tile_cols), cand_key, cand_col, cand_cnt, row_flag};
+    cudaStream_t s = as_stream(stream);
+    if (tile_cols == 128) {
+        const size_t smem = static_cast<size_t>(BB) * 129 * 4;
+        auto kern = vec4 ? dense_grad128_kernel<true, true> : dense_grad128_kernel<false, true>;
+        if (int rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                      static_cast<int>(smem)), fn))
+            return rc;
+        const dim3 g2(static_cast<unsigned>((K + BB - 1) / BB), static_cast<unsigned>((M + BB - 1) / BB));
+        kern<<<g2, kGThreads, smem, s>>>(dY, X, static_cast<int>(M), static_cast<int>(K), N, nullptr, ta);
+    } else {
+        auto kern = vec4 ? dense_grad_kernel<true, true> : dense_grad_kernel<false, true>;
+        const dim3 g(static_cast<unsigned>((K + BK - 1) / BK), static_cast<unsigned>((M + BM - 1) / BM));
+        kern<<<g, kGThreads, 0, s>>>(dY, X, static_cast<int>(M), static_cast<int>(K), N, nullptr, ta);
+    }
     SL_RETURN_IF_LAUNCH_FAILED(fn);
     return SL_OK;
 }
 
-extern "C" int sl_rigl_merge(int64_t M, int64_t K, int64_t lmax, const uint32_t* cand_key,
+extern "C" int sl_rigl_merge(int64_t M, int64_t K, int64_t lmax, int64_t tile_cols,
+                             const uint32_t* cand_key,
                              const int32_t* cand_col, const int32_t* cand_cnt,
                              const int32_t* n_grow, const int32_t* grow_offsets,
                              const int32_t* row_nnz, int32_t* row_flag, int32_t* row_mask,
                              int32_t* grow_cols, void* stream) {
     const char* fn = "sl_rigl_merge";
-    if (M < 0 || K < 1 || lmax < 1 || lmax > 128) return fail(SL_ERR_INVALID, std::string(fn) + ": bad arguments");
+    if (M < 0 || K < 1 || lmax < 1 || lmax > 128 || (tile_cols != 64 && tile_cols != 128))
+        return fail(SL_ERR_INVALID, std::string(fn) + ": bad arguments");
     if (M == 0) return SL_OK;
     SL_REQUIRE(cand_key && cand_col && cand_cnt && n_grow && grow_offsets && row_nnz && row_flag &&
                    row_mask && grow_cols,
                fn, "NULL argument");
     rigl_merge_kernel<<<row_grid(M), 256, 0, as_stream(stream)>>>(
-        static_cast<int>(M), static_cast<int>((K + BB - 1) / BB), static_cast<int>(lmax), cand_key,
+        static_cast<int>(M), static_cast<int>((K + tile_cols - 1) / tile_cols), static_cast<int>(lmax), cand_key,
         cand_col, cand_cnt, n_grow, grow_offsets, row_nnz, row_flag, row_mask, grow_cols);
     SL_RETURN_IF_LAUNCH_FAILED(fn);
     return SL_OK;

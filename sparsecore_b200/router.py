@@ -358,21 +358,22 @@ class RigL(DynamicSparsityAlgorithm):
         n_grow = torch.empty(M, dtype=torch.int32, device=dev)
         N.call("sl_rigl_prep", csr._abi_ref(), N.ptr(pr.thr), N.ptr(pr.force), N.ptr(bits),
                N.ptr(n_grow), s)
-        lmax = int(min(int(csr._rn_h.max()) + 1, 128))
-        tiles = (K + 127) // 128
+        tcols = int(N.lib().sl_rigl_tile_cols(M, K))
+        lmax = int(min(int(csr._rn_h.max()) + 1, tcols))
+        tiles = (K + tcols - 1) // tcols
         cand_key = torch.empty(M * tiles * lmax, dtype=torch.int32, device=dev)
         cand_col = torch.empty(M * tiles * lmax, dtype=torch.int32, device=dev)
         cand_cnt = torch.empty(M * tiles, dtype=torch.int32, device=dev)
         flags = torch.zeros(M, dtype=torch.int32, device=dev)
         N.call("sl_rigl_candidates", N.ptr(dYt), N.ptr(Xt), M, K, Nn, N.ptr(bits), N.ptr(n_grow),
-               lmax, N.ptr(cand_key), N.ptr(cand_col), N.ptr(cand_cnt), N.ptr(flags), s)
+               lmax, tcols, N.ptr(cand_key), N.ptr(cand_col), N.ptr(cand_cnt), N.ptr(flags), s)
         off = torch.zeros(M + 1, dtype=torch.int32, device=dev)
         total = torch.empty(1, dtype=torch.int64, device=dev)
         N.call("sl_exclusive_scan", N.ptr(n_grow), M, N.ptr(off), N.ptr(total), s)
         off[M:].copy_(total)  # grow lists of row i: [off[i], off[i + 1])
         grow = torch.empty(max(csr.nnz, 1), dtype=torch.int32, device=dev)  # >= sum(n_grow)
         mask = torch.empty(M, dtype=torch.int32, device=dev)
-        N.call("sl_rigl_merge", M, K, lmax, N.ptr(cand_key), N.ptr(cand_col), N.ptr(cand_cnt),
+        N.call("sl_rigl_merge", M, K, lmax, tcols, N.ptr(cand_key), N.ptr(cand_col), N.ptr(cand_cnt),
                N.ptr(n_grow), N.ptr(off), N.ptr(csr.row_nnz), N.ptr(flags), N.ptr(mask),
                N.ptr(grow), s)
         N.call("sl_dst_apply_cols", csr._abi_ref(), N.ptr(pr.thr), N.ptr(pr.force), N.ptr(mask),

@@ -2,7 +2,8 @@
 torch.optim.AdamW on the same model and data: equal to float rounding over
 several steps and across a SET topology update (per-slot state stays with
 the slot in both), padding slots stay exactly zero, and the dense
-parameters follow torch's AdamW exactly."""
+parameters follow torch's AdamW (to the same tolerance: their gradients
+see the sparse weights' rounding differences)."""
 import pytest
 import torch
 
@@ -45,7 +46,9 @@ def test_live_adamw_matches_torch_adamw_across_a_topology_update():
                 torch.testing.assert_close(m_b._values, m_a._values, rtol=1e-5, atol=1e-7)
                 pad = m_b._csr.col_indices < 0
                 assert bool((m_b._values[pad] == 0).all())
-    torch.testing.assert_close(b[3].weight, a[3].weight, rtol=0, atol=0)
+    # the dense layer follows torch's AdamW; its gradients see the sparse
+    # weights' rounding differences, so it agrees to the same tolerance
+    torch.testing.assert_close(b[3].weight, a[3].weight, rtol=1e-5, atol=1e-7)
     assert algo_b._step_idx == 9 and algo_b.last_update_step == 8
 
 

@@ -217,13 +217,17 @@ def test_rigl_fused_grow_matches_reference(golden, idx):
     W.assert_invariants()
 
 
+@pytest.mark.parametrize("tiling", ["64", "128"])
 @pytest.mark.parametrize("M,K,s,zero_rows", [(300, 700, 0.9, False), (1536, 384, 0.9, True),
                                              (200, 1100, 0.5, False)])
-def test_rigl_fused_grow_equals_materialised_path(M, K, s, zero_rows):
-    """Fused and materialised grow paths on random layers (several 128-column
-    tiles, ragged edges, long rows up to the 128-candidate cap), with rows of
-    all-zero gradient (every candidate ties: host path) mixed in."""
+def test_rigl_fused_grow_equals_materialised_path(M, K, s, zero_rows, tiling, monkeypatch):
+    """Fused and materialised grow paths on random layers (64- and 128-column
+    GEMM tiles, ragged edges, long rows beyond the per-tile candidate cap),
+    with rows of all-zero gradient (every candidate ties: host path) mixed
+    in."""
     import sparsecore_b200 as sl
+
+    monkeypatch.setenv("SPARSECORE_B200_DG", tiling)
 
     out = []
     for fused in (True, False):
