@@ -201,6 +201,7 @@ def run_sweep(args):
         for s in [float(v) for v in args.sweep_sparsity.split(",")]:
             W = _sweep_matrix(M, K, s)
             WT, _ = sl.transpose_with_perm(W)
+            cpu_timer = None  # the reference's CPU kernels on this matrix (built on first use)
             nnz = W.nnz
             for N in [int(v) for v in args.sweep_n.split(",")]:
                 if 4 * (K * N + M * N) * 3 > 60e9:
@@ -224,13 +225,15 @@ def run_sweep(args):
                                   "bound": "hbm" if hbm_floor >= fma_floor else "fp32-fma",
                                   "binding_frac": round(max(hbm_floor, fma_floor) / ms, 3)}
                 if 0 < N <= args.sweep_cpu_max_n:
-                    from oracle import oracle as O
-                    from oracle import ref_arm
+                    if cpu_timer is None:
+                        from oracle import oracle as O
+                        from oracle import ref_arm
 
-                    h = lambda t: t.detach().cpu().numpy().copy()  # noqa: E731
-                    p = O.CSR(M, K, h(W.values), h(W.col_indices), h(W.row_start), h(W.row_nnz),
-                              h(W.row_capacity))
-                    ct = ref_arm.kernel_times(p, X.cpu().numpy(), dY.cpu().numpy())
+                        h = lambda t: t.detach().cpu().numpy().copy()  # noqa: E731
+                        p = O.CSR(M, K, h(W.values), h(W.col_indices), h(W.row_start),
+                                  h(W.row_nnz), h(W.row_capacity))
+                        cpu_timer = ref_arm.KernelTimer(p)
+                    ct = cpu_timer.cell(X.cpu().numpy(), dY.cpu().numpy())
                     cell["cpu_ms"] = ct
                     cell["speedup_vs_cpu"] = {k: round(ct[k] / cell[k]["ms"], 1)
                                               for k in ("fwd", "dw", "dx")}

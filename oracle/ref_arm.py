@@ -155,25 +155,31 @@ def linear_factory(kern):
     return make
 
 
-def kernel_times(p: O.CSR, X: np.ndarray, dY: np.ndarray) -> dict:
-    """Host-core time of the reference's own kernels on one sweep cell, by
-    the reference's timing method (examples/profile_phase1_timing_table.py
-    :45-59): warm-up calls, then the median of 30 trials, cut to the median
-    of 3 for calls over 1 s (and to one warm-up for calls over 0.2 s).
-    Forward ``spmm_simd(W, X)``, SDDMM ``spmm_grad_w_simd(W, dY, X)`` and dX
-    ``spmm_simd(W^T, dY)`` run the compiled reference ``_core`` (kind
-    "reference"); the transpose is the reference's Python algorithm
-    (sparselab/layout.py:460), restated in numpy here (kind "port").
-    Milliseconds per call."""
-    import statistics
-    import time
+class KernelTimer:
+    """Host-core time of the reference's own kernels on the cells of one
+    matrix, by the reference's timing method (examples/
+    profile_phase1_timing_table.py:45-59): warm-up calls, then the median
+    of 30 trials, cut to the median of 3 for calls over 1 s (and to one
+    warm-up for calls over 0.2 s).  Forward ``spmm_simd(W, X)``, SDDMM
+    ``spmm_grad_w_simd(W, dY, X)`` and dX ``spmm_simd(W^T, dY)`` run the
+    compiled reference ``_core`` (kind "reference"); the transpose is the
+    reference's Python algorithm (sparselab/layout.py:460), restated in
+    numpy here (kind "port"), timed once per matrix.  Milliseconds per
+    call."""
 
-    kern = kernels()
-    W = kern.make(p)
-    pT, _ = O.transpose_with_perm(p)
-    WT = kern.make(pT)
+    def __init__(self, p: O.CSR):
+        self.kern = kernels()
+        self.p = p
+        self.W = self.kern.make(p)
+        pT, _ = O.transpose_with_perm(p)
+        self.WT = self.kern.make(pT)
+        self.transpose_ms = self._time(lambda: O.transpose_with_perm(p))
 
-    def timeit(fn):
+    @staticmethod
+    def _time(fn):
+        import statistics
+        import time
+
         t0 = time.perf_counter()
         fn()
         first = time.perf_counter() - t0
@@ -187,9 +193,16 @@ def kernel_times(p: O.CSR, X: np.ndarray, dY: np.ndarray) -> dict:
             ts.append(time.perf_counter() - t0)
         return round(statistics.median(ts) * 1e3, 4)
 
-    X = np.ascontiguousarray(X, np.float32)
-    dY = np.ascontiguousarray(dY, np.float32)
-    return {"fwd": timeit(lambda: kern.fwd(W, X)), "dw": timeit(lambda: kern.dw(W, dY, X)),
-            "dx": timeit(lambda: kern.fwd(WT, dY)),
-            "transpose": timeit(lambda: O.transpose_with_perm(p)),
-            "kind": kern.kind, "transpose_kind": "port"}
+    def cell(self, X: np.ndarray, dY: np.ndarray) -> dict:
+        X = np.ascontiguousarray(X, np.float32)
+        dY = np.ascontiguousarray(dY, np.float32)
+        k = self.kern
+        return {"fwd": self._time(lambda: k.fwd(self.W, X)),
+                "dw": self._time(lambda: k.dw(self.W, dY, X)),
+                "dx": self._time(lambda: k.fwd(self.WT, dY)),
+                "transpose": self.transpose_ms, "kind": k.kind, "transpose_kind": "port"}
+
+
+def kernel_times(p: O.CSR, X: np.ndarray, dY: np.ndarray) -> dict:
+    """One cell's reference CPU times (see KernelTimer)."""
+    return KernelTimer(p).cell(X, dY)

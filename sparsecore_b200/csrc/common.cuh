@@ -40,8 +40,10 @@ int launch_spmv_ws(const sl_csr* W, const float* X, int64_t K, float* Y, cudaStr
 int launch_gather32_fwd(const sl_csr* W, const float* X, float* Y, cudaStream_t s);
 int launch_gather32_sddmm(const sl_csr* W, const float* dY, const float* X, float* dW,
                           cudaStream_t s);
-// SPARSECORE_B200_N32=rows keeps N = 32 on the general kernels (tests).
+// SPARSECORE_B200_N32=rows keeps the N = 32 SDDMM on the general kernels;
+// =gather also sends the N = 32 forward to the staged kernel (tests).
 bool gather32_enabled();
+bool gather32_forced();
 
 constexpr int kWarp = 32;
 

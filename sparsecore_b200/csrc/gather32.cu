@@ -196,6 +196,11 @@ bool gather32_enabled() {
     return e == nullptr || e[0] != 'r';
 }
 
+bool gather32_forced() {
+    const char* e = std::getenv("SPARSECORE_B200_N32");
+    return e != nullptr && e[0] == 'g';
+}
+
 // Three chunks in flight per warp (12 KB of X rows); -1 when not applicable.
 int launch_gather32_fwd(const sl_csr* W, const float* X, float* Y, cudaStream_t s) {
     if (!g32_applies(W, X, Y)) return -1;

@@ -999,7 +999,11 @@ extern "C" int sl_spmm_fwd(const sl_csr* W, const float* X, int64_t K, int64_t N
         const int rc = try_lanerow(W, X, N, Y, s);
         if (rc >= 0) return rc;
     }
-    if (N == 32 && gather32_enabled()) {
+    // N = 32: the row-warp kernel (32-bit offsets) measured faster than the
+    // cp.async-staged gather (4096^2 at 90%: 27.3 vs 31.9 us; L1 hits on the
+    // gathered X rows, which cp.async.cg bypasses); SPARSECORE_B200_N32=gather
+    // selects the staged kernel (tests).
+    if (N == 32 && gather32_forced()) {
         const int rc = launch_gather32_fwd(W, X, Y, s);
         if (rc >= 0) return rc;
     }

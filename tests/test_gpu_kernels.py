@@ -320,8 +320,9 @@ def test_lanerow_small_n_matches_oracle_and_warp_kernel(M, K, s, pr, monkeypatch
 
 @pytest.mark.parametrize("M,K,s", [(301, 517, 0.9), (2000, 4096, 0.95), (50, 70, 0.0)])
 def test_n32_gather_kernels_vs_oracle(M, K, s, monkeypatch):
-    """N = 32: the forward / dX and SDDMM kernels that stage X rows by
-    cp.async, against the oracle and the general kernels: empty rows, rows of
+    """N = 32: the SDDMM (default) and forward (forced) kernels that stage X
+    rows by cp.async, and the row-warp forward, against the oracle and each
+    other: empty rows, rows of
     exactly 32 / 33 / 64 slots (chunk edges) and one long row, so the
     register ring and the staging ring both wrap."""
     import sparsecore_b200 as sl
@@ -346,7 +347,12 @@ def test_n32_gather_kernels_vs_oracle(M, K, s, monkeypatch):
     X = torch.randn(K, 32, generator=g)
     dY = torch.randn(M, 32, generator=g)
     y, names = launched_kernels(lambda: sl.spmm(W, X.to(d)))
+    assert names == ["spmm_rowwarp_kernel"], names  # the N = 32 forward default
+    monkeypatch.setenv("SPARSECORE_B200_N32", "gather")
+    y_staged, names = launched_kernels(lambda: sl.spmm(W, X.to(d)))
     assert names == ["gather32_fwd_kernel"], names
+    assert bits_equal(y_staged, y)
+    monkeypatch.delenv("SPARSECORE_B200_N32")
     dw, names = launched_kernels(lambda: ops._sddmm_raw(W, dY.to(d), X.to(d)))
     assert names == ["gather32_sddmm_kernel"], names
     dx = ops._spmm_raw(WT, dY.to(d))
