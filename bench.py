@@ -51,6 +51,8 @@ def parse():
                     help="stream for the training step: a high-priority stream (default; the "
                          "weight-gradient SDDMM side stream keeps the lowest priority, so "
                          "critical-path kernels get SMs first) or torch's default stream")
+    ap.add_argument("--probe", action="store_true",
+                    help="only measure the FP32 and shared-memory ceilings (probe kernels)")
     ap.add_argument("--sweep", action="store_true",
                     help="config-3 standalone SpMM sweep: one JSON line per cell")
     ap.add_argument("--flush", choices=["read", "write"], default="write",
@@ -694,6 +696,11 @@ def main():
         sys.path.insert(0, REPO)
     if args.kernel:
         run_kernel_case(args.kernel)
+        return
+    if args.probe:
+        from sparsecore_b200 import _native as N
+
+        print(json.dumps({"measured_ceilings": N.measure_ceilings()}), flush=True)
         return
     if args.sweep:
         FLUSH_MODE["mode"] = args.flush

@@ -4,9 +4,10 @@
 //  * sl_probe_ffma: every thread advances 8 independent FMA chains for
 //    `iters` steps (2 * 8 * iters FLOPs per thread); one CTA of 256 threads
 //    per 64 resident warps' worth of work on every SM.
-//  * sl_probe_smem: every thread reads `iters` conflict-free 128-bit words
-//    from shared memory (a warp covers 512 contiguous bytes per load), so
-//    the bytes moved are 16 * iters per thread.
+//  * sl_probe_smem: every thread reads 4 * `iters` conflict-free 128-bit
+//    words from shared memory (a warp covers 512 contiguous bytes per load;
+//    each address depends on the previous load, so none can be removed), so
+//    the bytes moved are 64 * iters per thread.
 // Both write one value per thread to `out` so nothing is optimised away.
 #include "common.cuh"
 
@@ -29,24 +30,27 @@ __global__ void __launch_bounds__(256) probe_ffma_kernel(int64_t iters, float se
 }
 
 __global__ void __launch_bounds__(256) probe_smem_kernel(int64_t iters, float* out) {
+    // Every value in the buffer is 0, but the compiler cannot know it: each
+    // load's address adds the previous load's value, so no load can be
+    // hoisted or merged, and four independent chains per thread keep loads
+    // in flight.  A warp's load covers 512 contiguous bytes (conflict-free).
     __shared__ __align__(16) float4 buf[1024];  // 16 KB
-    for (int k = threadIdx.x; k < 1024; k += blockDim.x)
-        buf[k] = make_float4(k, k + 1, k + 2, k + 3);
+    for (int k = threadIdx.x; k < 1024; k += blockDim.x) buf[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     __syncthreads();
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(buf));
-    uint32_t off = (threadIdx.x & 1023) * 16;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int idx[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) idx[c] = (warp * 4 + c) * 32 % 1024 + lane;
+    float s = 0.0f;
     for (int64_t i = 0; i < iters; ++i) {
-        float4 v;
-        // volatile: every iteration's load is issued (the addresses repeat
-        // every 4 iterations, which a compiler could otherwise hoist).
-        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                     : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                     : "r"(base + off));
-        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
-        off = (off + 4096) & 16383;  // consecutive lanes, consecutive 16-byte words
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const float4 v = buf[idx[c]];
+            s += v.w;
+            idx[c] = ((idx[c] + 256 + __float_as_int(v.x)) & 1023);
+        }
     }
-    out[blockIdx.x * blockDim.x + threadIdx.x] = acc.x + acc.y + acc.z + acc.w;
+    out[blockIdx.x * blockDim.x + threadIdx.x] = s;
 }
 
 }  // namespace
