@@ -61,7 +61,7 @@ SL_API const char* sl_last_kernel(void);
 /* Roofline probes (no reference counterpart): sl_probe_ffma runs
  * sl_probe_threads() threads, each advancing 8 independent fp32 FMA chains
  * for `iters` steps (16 * iters FLOPs per thread); sl_probe_smem has the same
- * threads each read 4 * `iters` conflict-free 16-byte shared-memory words
+ * threads each read 4 * `iters` conflict-free 8-byte shared-memory words
  * (each address depends on the previous load, so none is optimised away).
  * `out` receives one float per thread (sl_probe_threads() floats).  Timed by
  * the caller (CUDA events) to give the measured FP32 and shared-memory

@@ -233,10 +233,10 @@ def measure_ceilings(device: torch.device | None = None) -> dict:
     ms_f = best_ms("sl_probe_ffma", it_f)
     ms_s = best_ms("sl_probe_smem", it_s)
     fp32 = 16.0 * it_f * n / (ms_f * 1e-3) / 1e12
-    smem = 64.0 * it_s * n / (ms_s * 1e-3) / 1e12
+    smem = 32.0 * it_s * n / (ms_s * 1e-3) / 1e12
     return {"fp32_tflops": round(fp32, 2), "smem_tbs": round(smem, 2),
             "gather_ceiling_tflops": round(smem / 4.0 * 2.0, 2),
             "how": "library probe kernels (sl_probe_ffma: 8 independent FMA chains per thread; "
-                   "sl_probe_smem: conflict-free 128-bit shared loads with data-dependent addresses), "
+                   "sl_probe_smem: conflict-free 64-bit shared loads with data-dependent addresses), "
                    "64 warps per SM, "
                    "CUDA events, best of 5; gather ceiling = 4 B of shared/L1 operand per FMA"}
