@@ -350,6 +350,11 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
 
     if (producer) {
         if (lane == 0) {
+            // The operand the resident CTAs share is streamed once (evict
+            // first); the other one is re-read by the later bands of tiles
+            // and should stay in L2 (evict last).
+            const uint64_t pol_rows = col_major ? l2_policy_evict_last() : l2_policy_evict_first();
+            const uint64_t pol_cols = col_major ? l2_policy_evict_first() : l2_policy_evict_last();
             const unsigned chunk_bytes = static_cast<unsigned>(stage * 4);
             unsigned eph = 0u;  // bit b = parity of stage b's next release
             int g = 0;
@@ -362,8 +367,8 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
                 const int k = g % nchunks;
                 fence_proxy_async();
                 mbar_expect_tx(&full[b], chunk_bytes);
-                tma_load_2d(sbase + b * stage, &dymap, k * kTJ, r0, &full[b]);
-                tma_load_2d(sbase + b * stage + TR * kTJ, &xmap, k * kTJ, c0, &full[b]);
+                tma_load_2d_hint(sbase + b * stage, &dymap, k * kTJ, r0, &full[b], pol_rows);
+                tma_load_2d_hint(sbase + b * stage + TR * kTJ, &xmap, k * kTJ, c0, &full[b], pol_cols);
             }
             // Before the CTA may exit, every issued copy must have landed:
             // wait (bounded) for the full-barrier completion of the last
