@@ -4,11 +4,18 @@ The reference has no distributed path; this adds the one the benchmark
 needs.  Every rank holds a full replica with the same topology; the batch is
 sharded.  Per step:
 
-* ``allreduce_grads()`` -- ONE collective: the live-slot gradients of every
-  SparseLinear (packed out of the padded ``total_capacity`` layout by
-  ``sl_pack_live``; padding never travels) and all dense gradients are
-  concatenated into one flat fp32 bucket, all-reduced with ReduceOp.AVG and
-  scattered back (``sl_unpack_live``).
+* ``allreduce_grads()`` -- the live-slot gradients of every SparseLinear
+  (packed out of the padded ``total_capacity`` layout by ``sl_pack_live``;
+  padding never travels) and all dense gradients are concatenated into one
+  flat fp32 buffer, all-reduced with ReduceOp.AVG and scattered back
+  (``sl_unpack_live``).  With ``overlap=True`` (and the library's async
+  weight-gradient mode on) the sparse part is split into buckets of about
+  ``bucket_mb`` in backward order; each layer's gradient is packed on the
+  weight-gradient side stream as soon as its SDDMM is enqueued, and a
+  bucket's all-reduce is launched there when its last layer is packed, so
+  the exchange runs while the rest of the backward pass does.
+  ``allreduce_grads()`` then only waits for the buckets, unpacks them and
+  exchanges the small dense part.
 * after a router update, ``broadcast_topology(src=0)`` sends rank 0's
   ``col_indices`` / ``row_nnz`` / ``values`` of every layer (one flat int32
   and one flat fp32 broadcast) plus the topology versions, so all replicas
@@ -68,7 +75,8 @@ class SparseDataParallel:
 
     def __init__(self, model: torch.nn.Module, process_group=None,
                  pack: Callable | None = None, unpack: Callable | None = None,
-                 offsets: Callable | None = None, sparse_layers: list | None = None):
+                 offsets: Callable | None = None, sparse_layers: list | None = None,
+                 overlap: bool = False, bucket_mb: float = 8.0):
         from .nn import SparseLinear
 
         self.model = model
@@ -85,6 +93,19 @@ class SparseDataParallel:
         self._plan: list[_Slot] = []
         self._bucket: torch.Tensor | None = None
         self._offsets: dict[int, torch.Tensor] = {}
+        # overlapped exchange state
+        self.overlap = bool(overlap)
+        self.bucket_bytes = int(bucket_mb * 2 ** 20)
+        self._slot_of: dict[int, _Slot] = {}      # id(param) -> slot
+        self._bucket_of: dict[int, int] = {}      # id(param) -> bucket index
+        self._bucket_ranges: list[tuple[int, int, int]] = []  # (offset, length, n_layers)
+        self._packed: dict[int, int] = {}         # bucket -> layers packed this step
+        self._works: list = []
+        self._packed_params: set = set()
+        if self.overlap:
+            from . import ops
+
+            ops.add_weight_grad_hook(self._on_weight_grad)
 
     # ── planning ────────────────────────────────────────────────────────
     def _key(self):
@@ -95,9 +116,23 @@ class SparseDataParallel:
         if key == self._plan_key:
             return self._plan
         slots, off = [], 0
-        for m in self.sparse_layers:
-            slots.append(_Slot("sparse", m, m._values, off, m._csr.nnz))
+        # Sparse layers in backward order (their gradients arrive in that
+        # order), then the dense parameters; buckets are contiguous ranges.
+        self._bucket_ranges, self._bucket_of, self._slot_of = [], {}, {}
+        b_off, b_len, b_n = 0, 0, 0
+        for m in reversed(self.sparse_layers):
+            sl = _Slot("sparse", m, m._values, off, m._csr.nnz)
+            slots.append(sl)
+            self._slot_of[id(m._values)] = sl
+            self._bucket_of[id(m._values)] = len(self._bucket_ranges)
             off += m._csr.nnz
+            b_len += m._csr.nnz
+            b_n += 1
+            if 4 * b_len >= self.bucket_bytes:
+                self._bucket_ranges.append((b_off, b_len, b_n))
+                b_off, b_len, b_n = off, 0, 0
+        if b_n:
+            self._bucket_ranges.append((b_off, b_len, b_n))
         for p in self.dense_params:
             slots.append(_Slot("dense", None, p, off, p.numel()))
             off += p.numel()
@@ -116,11 +151,80 @@ class SparseDataParallel:
     def world_size(self) -> int:
         return dist.get_world_size(self.pg) if dist.is_available() and dist.is_initialized() else 1
 
+    # ── overlapped exchange ─────────────────────────────────────────────
+    def _on_weight_grad(self, param, dW) -> None:
+        """Called on the weight-gradient side stream right after a layer's
+        SDDMM: pack its live slots into its bucket and, once the bucket is
+        complete, launch the bucket's all-reduce there."""
+        if self.world_size() == 1 or torch.cuda.is_current_stream_capturing():
+            return
+        self.plan()
+        sl = self._slot_of.get(id(param))
+        if sl is None:
+            return
+        b = self._bucket_of[id(param)]
+        off, length, n = self._bucket_ranges[b]
+        self._pack(sl.module, self._offsets[id(sl.module)], dW, self._bucket[sl.offset:sl.offset + sl.length])
+        self._packed_params.add(id(param))
+        self._packed[b] = self._packed.get(b, 0) + 1
+        if self._packed[b] == n:
+            view = self._bucket[off:off + length]
+            if dist.get_backend(self.pg) == "nccl":
+                w = dist.all_reduce(view, op=dist.ReduceOp.AVG, group=self.pg, async_op=True)
+            else:
+                w = dist.all_reduce(view, op=dist.ReduceOp.SUM, group=self.pg, async_op=True)
+            self._works.append((w, view))
+
+    def _finish_overlapped(self, slots, world) -> bool:
+        """Wait for the buckets launched during backward and unpack them; the
+        dense part goes through one all-reduce here.  False when the
+        backward did not pack every sparse layer (e.g. the synchronous
+        weight-gradient mode): the caller then exchanges everything."""
+        sparse = [s for s in slots if s.kind == "sparse"]
+        ok = len(self._packed_params) == len(sparse) and len(self._works) == len(self._bucket_ranges)
+        if not ok:
+            for w, _ in self._works:
+                w.wait()
+            self._works, self._packed, self._packed_params = [], {}, set()
+            return False
+        nccl = dist.get_backend(self.pg) == "nccl"
+        for w, view in self._works:
+            w.wait()
+            if not nccl:
+                view.div_(world)
+        for s in sparse:
+            view = self._bucket[s.offset:s.offset + s.length]
+            if s.param.grad is None:
+                s.param.grad = torch.zeros_like(s.param)
+            self._unpack(s.module, self._offsets[id(s.module)], view, s.param.grad)
+        self._works, self._packed, self._packed_params = [], {}, set()
+        dense = [s for s in slots if s.kind == "dense"]
+        if dense:
+            d0 = dense[0].offset
+            buf = self._bucket[d0:]
+            for s in dense:
+                view = self._bucket[s.offset:s.offset + s.length]
+                view.copy_(s.param.grad.reshape(-1)) if s.param.grad is not None else view.zero_()
+            if nccl:
+                dist.all_reduce(buf, op=dist.ReduceOp.AVG, group=self.pg)
+            else:
+                dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=self.pg)
+                buf.div_(world)
+            for s in dense:
+                view = self._bucket[s.offset:s.offset + s.length]
+                if s.param.grad is None:
+                    s.param.grad = torch.zeros_like(s.param)
+                s.param.grad.copy_(view.view_as(s.param.grad))
+        return True
+
     def allreduce_grads(self) -> None:
         world = self.world_size()
         if world == 1:
             return
         slots = self.plan()
+        if self.overlap and (self._works or self._packed_params):
+            if self._finish_overlapped(slots, world):
+                return
         buf = self._bucket
         for s in slots:
             view = buf[s.offset:s.offset + s.length]

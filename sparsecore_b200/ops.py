@@ -237,6 +237,21 @@ class _SparseLinearFunction(torch.autograd.Function):
 # plain autograd semantics.
 _async_weight_grad = False
 _side_streams: dict = {}
+# Callables (param, dW) run on the side stream right after a SparseLinear's
+# SDDMM is enqueued there (async weight-gradient mode only); the data-
+# parallel helper packs and all-reduces gradient buckets from here, so the
+# exchange overlaps the rest of the backward pass.
+_weight_grad_hooks: list = []
+
+
+def add_weight_grad_hook(fn) -> None:
+    if fn not in _weight_grad_hooks:
+        _weight_grad_hooks.append(fn)
+
+
+def remove_weight_grad_hook(fn) -> None:
+    if fn in _weight_grad_hooks:
+        _weight_grad_hooks.remove(fn)
 
 
 def set_async_weight_grad(enabled: bool) -> None:
@@ -277,6 +292,8 @@ def _sddmm_on_side_stream(W: PaddedCSR, dY: torch.Tensor, X: torch.Tensor, param
     side.wait_stream(main)
     with torch.cuda.stream(side):
         dW = _sddmm_raw(W, dY, X)
+        for hook in _weight_grad_hooks:
+            hook(param, dW)
         done = torch.cuda.Event()
         done.record(side)
     capturing = torch.cuda.is_current_stream_capturing()

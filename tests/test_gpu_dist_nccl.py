@@ -46,7 +46,7 @@ def _world1():
     return losses
 
 
-def _rank(rank, world, port, q):
+def _rank(rank, world, port, q, overlap=False):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
         torch.cuda.set_device(rank)
@@ -59,7 +59,11 @@ def _rank(rank, world, port, q):
         model, algo, opt, x, y = _setup(dev)
         shard = BATCH // world
         xs, ys = x[rank * shard:(rank + 1) * shard].to(dev), y[rank * shard:(rank + 1) * shard].to(dev)
-        ddp = SparseDataParallel(model)
+        if overlap:
+            from sparsecore_b200 import ops
+
+            ops.set_async_weight_grad(True)  # packs + bucket all-reduces start during backward
+        ddp = SparseDataParallel(model, overlap=overlap, bucket_mb=0.01)
         losses = []
         for _ in range(STEPS):
             opt.zero_grad(set_to_none=True)
@@ -85,12 +89,16 @@ def _free_port():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_gpu_data_parallel_matches_one_gpu():
+@pytest.mark.parametrize("overlap", [False, True])
+def test_two_gpu_data_parallel_matches_one_gpu(overlap):
+    """overlap=True: per-layer packs and bucketed all-reduces launched from
+    the weight-gradient side stream during backward (buckets of ~10 KB here,
+    so each layer is its own bucket)."""
     want = _world1()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q, overlap)) for r in range(2)]
     for p in procs:
         p.start()
     out = {}
