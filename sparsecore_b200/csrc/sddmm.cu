@@ -288,7 +288,7 @@ __device__ __forceinline__ int consumer_exclusive_scan(int v, int* ws, int* tota
 
 __global__ void __launch_bounds__(kTThreads + 32, 2)
 sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_constant__ CUtensorMap xmap,
-                   int M, int64_t N, int TR, int TC, int n_bc, int n_bi, int col_major,
+                   int M, int64_t N, int TR, int TC, int n_bc, int n_bi, int col_major, int shared_first,
                    const int32_t* __restrict__ row_start, const int32_t* __restrict__ row_nnz,
                    const int32_t* __restrict__ row_capacity, const int32_t* __restrict__ cols,
                    float* __restrict__ dW, unsigned* status) {
@@ -353,8 +353,9 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
             // The operand the resident CTAs share is streamed once (evict
             // first); the other one is re-read by the later bands of tiles
             // and should stay in L2 (evict last).
-            const uint64_t pol_rows = col_major ? l2_policy_evict_last() : l2_policy_evict_first();
-            const uint64_t pol_cols = col_major ? l2_policy_evict_first() : l2_policy_evict_last();
+            const uint64_t shared = shared_first ? l2_policy_evict_first() : l2_policy_evict_normal();
+            const uint64_t pol_rows = col_major ? l2_policy_evict_last() : shared;
+            const uint64_t pol_cols = col_major ? shared : l2_policy_evict_last();
             const unsigned chunk_bytes = static_cast<unsigned>(stage * 4);
             unsigned eph = 0u;  // bit b = parity of stage b's next release
             int g = 0;
@@ -581,9 +582,13 @@ int try_tiled(const sl_csr* W, const float* dY, const float* X, int64_t N, float
     int col_major = K > M ? 1 : 0;  // X (K x N) is the larger operand
     if (const char* e = std::getenv("SPARSECORE_B200_DW_ORDER"))  // row|col (measurements)
         col_major = e[0] == 'c' ? 1 : 0;
+    // L2 policy of the operand the resident CTAs share: evict-first (its
+    // bytes are read once) or normal (SPARSECORE_B200_DW_L2=first|normal).
+    int shared_first = 1;
+    if (const char* e = std::getenv("SPARSECORE_B200_DW_L2")) shared_first = e[0] == 'f' ? 1 : 0;
     note_kernel("sddmm_tiled_kernel");
     kern<<<n_bi * n_bc, kTThreads + 32, smem, s>>>(
-        dymap, xmap, static_cast<int>(M), N, TR, TC, n_bc, n_bi, col_major, W->row_start,
+        dymap, xmap, static_cast<int>(M), N, TR, TC, n_bc, n_bi, col_major, shared_first, W->row_start,
         W->row_nnz, W->row_capacity, W->col_indices, dW, status);
     SL_RETURN_IF_LAUNCH_FAILED("sl_sddmm_dw (tiled)");
     return SL_OK;

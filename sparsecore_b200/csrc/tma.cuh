@@ -97,6 +97,12 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
     return p;
 }
 
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 // TMA 2-D tile load with an L2 cache policy (see above).
 __device__ __forceinline__ void tma_load_2d_hint(void* smem_dst, const CUtensorMap* map, int x, int y,
                                                  uint64_t* bar, uint64_t policy) {
