@@ -715,13 +715,16 @@ def main():
         line = run_reference(args, rank, world)
     else:
         if world > 1:
-            # NCCL's communicator set-up lines (ranks, transport) on stderr;
-            # stdout keeps the one JSON line.
-            os.environ.setdefault("NCCL_DEBUG", "INFO")
-            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
-            os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
             torch.cuda.set_device(local_rank)
             dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+            # One communicator line per rank on stderr (stdout keeps the one
+            # JSON line): which rank runs on which GPU over which NCCL.
+            probe = torch.ones(1, device=torch.device("cuda", local_rank))
+            dist.all_reduce(probe)
+            ver = ".".join(str(v) for v in torch.cuda.nccl.version())
+            print(f"NCCL communicator: rank {rank} of {world} on cuda:{local_rank} "
+                  f"({torch.cuda.get_device_name(local_rank)}), NCCL {ver}, all-reduce check "
+                  f"{int(probe.item())} == {world}", file=sys.stderr, flush=True)
         line = run_ours(args, rank, world, local_rank)
         if world > 1:
             dist.barrier()
