@@ -402,10 +402,10 @@ def run_ours(args, rank, world, local_rank):
     wl = Workload(args.workload, dev, rank, capturable=args.graph)
     model, algo, opt = wl.model, wl.algo, wl.opt
     ops.set_async_weight_grad(True)  # the loop below reads .grad after backward()
-    # Bucketed exchange overlapped with the backward pass (needs the async
-    # weight-gradient mode set above; the serial timing pass below falls back
-    # to the single post-backward exchange, which is what it times).
-    ddp = SparseDataParallel(model, overlap=True)
+    # One batched exchange after the backward pass.  (The bucketed exchange
+    # overlapped with backward, overlap=True, measured no faster at 2 GPUs:
+    # 111.1 vs 110.7 ms per step.)
+    ddp = SparseDataParallel(model)
     batch_host = tuple(t.pin_memory() for t in wl.batch)
     batch_dev = tuple(t.to(dev) for t in batch_host)
 
@@ -587,11 +587,10 @@ def run_ours(args, rank, world, local_rank):
             "bucket_bytes": ddp.bucket_numel * 4,
             "ms_per_step": round(exchange_ms, 3),
             "share_of_step": round(exchange_ms / (t_ms / args.steps), 4),
-            "what": ("timed steps: sparse dW packed per layer and all-reduced in ~8 MB buckets on "
-                     "the weight-gradient side stream during backward, dense grads after it; "
-                     "ms_per_step times the non-overlapped exchange (pack everything, one NCCL "
-                     "all-reduce AVG, unpack) with CUDA events in the serial pass, max over "
-                     "ranks") if world > 1 else "single GPU: no exchange"},
+            "what": ("one pack launch for every sparse layer's live dW slots, one concatenation "
+                     "of the dense grads, one NCCL all-reduce (AVG), one unpack launch, one "
+                     "multi-tensor copy back; CUDA events around allreduce_grads() in the serial "
+                     "pass, max over ranks") if world > 1 else "single GPU: no exchange"},
         "router": {"algorithm": type(algo).__name__, "every_steps": algo.update_freq,
                    "update_plus_broadcast_ms": round(router_ms, 1),
                    "note": "no update falls inside the timed window; amortised cost per step = "

@@ -316,6 +316,26 @@ SL_API int sl_pack_live(const sl_csr* W, const int32_t* packed_offsets,
                  const float* src, float* dst, void* stream);
 SL_API int sl_unpack_live(const sl_csr* W, const int32_t* packed_offsets,
                    const float* src, float* dst, float scale, void* stream);
+/* Batched pack / unpack of many layers' live gradient slots in one launch
+ * (the per-layer calls above, fused; no reference counterpart).  `descs`
+ * is a DEVICE array of n_descs descriptors; descriptor i owns launch blocks
+ * [first_block_i, first_block_{i+1}) with first_block_0 = 0 and
+ * ceil(nrows_i / 8) blocks each; n_blocks is the total.  pack copies
+ * grad[row_start[r] + k] (k < row_nnz[r]) to
+ * bucket[bucket_offset + packed_offsets[r] + k]; unpack copies back. */
+typedef struct sl_live_desc {
+    const int32_t* row_start;
+    const int32_t* row_nnz;
+    const int32_t* packed_offsets;
+    float* grad;
+    int64_t nrows;
+    int64_t bucket_offset;
+    int64_t first_block;
+} sl_live_desc;
+SL_API int sl_pack_live_batch(const sl_live_desc* descs, int64_t n_descs, int64_t n_blocks,
+                       float* bucket, void* stream);
+SL_API int sl_unpack_live_batch(const sl_live_desc* descs, int64_t n_descs, int64_t n_blocks,
+                         const float* bucket, void* stream);
 /* Exclusive scan of int32 counts (n <= 2^31 total) into out[n];
  * *total_dev (device int64) receives the sum. */
 SL_API int sl_exclusive_scan(const int32_t* counts, int64_t n, int32_t* out,

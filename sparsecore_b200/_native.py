@@ -77,6 +77,8 @@ SIGNATURES: dict[str, tuple] = {
     "sl_adamw_live": (I32, [P, P, P, P, F32, F32, F32, F32, F32, I64, P]),
     "sl_unpack_live": (I32, [P, P, P, P, F32, P]),
     "sl_exclusive_scan": (I32, [P, I64, P, P, P]),
+    "sl_pack_live_batch": (I32, [P, I64, I64, P, P]),
+    "sl_unpack_live_batch": (I32, [P, I64, I64, P, P]),
     "sl_transpose_f32": (I32, [P, I64, I64, P, P]),
     "sl_set_regrow_draws": (I32, [P, P, P, I64, P, P, I64, P, P, I64, P]),
 }
@@ -146,7 +148,8 @@ KERNELS_PER_CALL = {
     "sl_values_gather": 1, "sl_dense_count": 2, "sl_dense_fill": 1, "sl_capacity_scan": 1,
     "sl_to_dense": 1, "sl_check_invariants": 2, "sl_dense_grad": 1, "sl_rigl_prep": 1, "sl_rigl_candidates": 1, "sl_rigl_merge": 1, "sl_dst_threshold": 9,
     "sl_dst_keep": 1, "sl_dst_apply_random": 1, "sl_dst_apply_topk": 1, "sl_dst_apply_cols": 1,
-    "sl_pack_live": 1, "sl_unpack_live": 1, "sl_adamw_live": 1, "sl_exclusive_scan": 1,
+    "sl_pack_live": 1, "sl_unpack_live": 1, "sl_adamw_live": 1, "sl_pack_live_batch": 1,
+    "sl_unpack_live_batch": 1, "sl_exclusive_scan": 1,
     "sl_set_regrow_draws": 0,  # host only
     "sl_probe_ffma": 1, "sl_probe_smem": 1,
 }

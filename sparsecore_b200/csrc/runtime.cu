@@ -127,6 +127,31 @@ unpack_live_kernel(int M, const int32_t* __restrict__ row_start,
     }
 }
 
+// Batched form: descriptor d covers blocks [d.first_block, next first
+// block); each block of 8 warps takes 8 rows of its layer.
+__device__ __forceinline__ int find_desc(const sl_live_desc* __restrict__ d, int64_t n, int64_t blk) {
+    int lo = 0, hi = static_cast<int>(n);
+    while (hi - lo > 1) {  // last descriptor whose first_block <= blk
+        const int mid = (lo + hi) >> 1;
+        if (d[mid].first_block <= blk) lo = mid; else hi = mid;
+    }
+    return lo;
+}
+
+template <bool PACK>
+__global__ void __launch_bounds__(256)
+live_batch_kernel(const sl_live_desc* __restrict__ descs, int64_t n, float* __restrict__ bucket) {
+    const sl_live_desc& d = descs[find_desc(descs, n, blockIdx.x)];
+    const int64_t row = (static_cast<int64_t>(blockIdx.x) - d.first_block) * 8 + (threadIdx.x >> 5);
+    if (row >= d.nrows) return;
+    const int rs = d.row_start[row], nn = d.row_nnz[row];
+    float* b = bucket + d.bucket_offset + d.packed_offsets[row];
+    for (int k = threadIdx.x & 31; k < nn; k += 32) {
+        if (PACK) b[k] = d.grad[rs + k];
+        else d.grad[rs + k] = b[k];
+    }
+}
+
 bool make_tmap_2d(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int box_rows,
                   int box_cols, bool swizzle128) {
     static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
@@ -266,6 +291,31 @@ int sl_unpack_live(const sl_csr* W, const int32_t* packed_offsets, const float* 
         static_cast<int>(W->nrows), W->row_start, W->row_nnz, packed_offsets, src, dst, scale);
     SL_RETURN_IF_LAUNCH_FAILED("sl_unpack_live");
     return SL_OK;
+}
+
+static int live_batch(const sl_live_desc* descs, int64_t n, int64_t n_blocks, float* bucket,
+                      void* stream, bool pack, const char* fn) {
+    if (n < 0 || n_blocks < 0) return fail(SL_ERR_INVALID, std::string(fn) + ": negative count");
+    if (n == 0 || n_blocks == 0) return SL_OK;
+    SL_REQUIRE(descs != nullptr && bucket != nullptr, fn, "NULL descriptors or bucket");
+    if (n_blocks > INT_MAX) return fail(SL_ERR_UNSUPPORTED, std::string(fn) + ": too many blocks");
+    if (pack)
+        live_batch_kernel<true><<<static_cast<unsigned>(n_blocks), 256, 0, as_stream(stream)>>>(descs, n, bucket);
+    else
+        live_batch_kernel<false><<<static_cast<unsigned>(n_blocks), 256, 0, as_stream(stream)>>>(descs, n, bucket);
+    SL_RETURN_IF_LAUNCH_FAILED(fn);
+    return SL_OK;
+}
+
+int sl_pack_live_batch(const sl_live_desc* descs, int64_t n_descs, int64_t n_blocks, float* bucket,
+                       void* stream) {
+    return live_batch(descs, n_descs, n_blocks, bucket, stream, true, "sl_pack_live_batch");
+}
+
+int sl_unpack_live_batch(const sl_live_desc* descs, int64_t n_descs, int64_t n_blocks,
+                         const float* bucket, void* stream) {
+    return live_batch(descs, n_descs, n_blocks, const_cast<float*>(bucket), stream, false,
+                      "sl_unpack_live_batch");
 }
 
 }  // extern "C"

@@ -225,6 +225,9 @@ class SparseDataParallel:
         if self.overlap and (self._works or self._packed_params):
             if self._finish_overlapped(slots, world):
                 return
+        if self._pack is _gpu_pack and self._unpack is _gpu_unpack:
+            self._exchange_batched(slots, world)
+            return
         buf = self._bucket
         for s in slots:
             view = buf[s.offset:s.offset + s.length]
@@ -249,6 +252,55 @@ class SparseDataParallel:
                 self._unpack(s.module, self._offsets[id(s.module)], view, s.param.grad)
             else:
                 s.param.grad.copy_(view.view_as(s.param.grad))
+
+    def _live_descs(self, sparse) -> tuple[torch.Tensor, int]:
+        """Device table of sl_live_desc for the sparse slots (their current
+        .grad tensors) and the launch's block count."""
+        import numpy as np
+
+        rows, blocks = [], 0
+        for s in sparse:
+            csr = s.module._csr
+            rows.append((csr.row_start.data_ptr(), csr.row_nnz.data_ptr(),
+                         self._offsets[id(s.module)].data_ptr(), s.param.grad.data_ptr(),
+                         csr.nrows, s.offset, blocks))
+            blocks += (csr.nrows + 7) // 8
+        arr = np.array(rows, dtype=np.int64).reshape(-1)
+        return torch.from_numpy(arr).to(self._bucket.device), blocks
+
+    def _exchange_batched(self, slots, world) -> None:
+        """The exchange with one pack launch for every sparse layer, one
+        concatenation of the dense gradients, one all-reduce, one unpack
+        launch and one multi-tensor copy back (instead of a pack, a copy and
+        an unpack per tensor)."""
+        buf = self._bucket
+        sparse = [s for s in slots if s.kind == "sparse"]
+        dense = [s for s in slots if s.kind == "dense"]
+        for s in sparse:
+            if s.param.grad is None:
+                s.param.grad = torch.zeros_like(s.param)
+        stream = N.stream_ptr(buf.device)
+        descs, blocks = self._live_descs(sparse) if sparse else (None, 0)
+        if sparse:
+            N.call("sl_pack_live_batch", N.ptr(descs), len(sparse), blocks, N.ptr(buf), stream)
+        if dense:
+            d0 = dense[0].offset
+            torch.cat([s.param.grad.reshape(-1) if s.param.grad is not None
+                       else torch.zeros(s.length, device=buf.device) for s in dense],
+                      out=buf[d0:d0 + sum(s.length for s in dense)])
+        if dist.get_backend(self.pg) == "nccl":
+            dist.all_reduce(buf, op=dist.ReduceOp.AVG, group=self.pg)
+        else:
+            dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=self.pg)
+            buf.div_(world)
+        if sparse:
+            N.call("sl_unpack_live_batch", N.ptr(descs), len(sparse), blocks, N.ptr(buf), stream)
+        if dense:
+            for s in dense:
+                if s.param.grad is None:
+                    s.param.grad = torch.zeros_like(s.param)
+            torch._foreach_copy_([s.param.grad.view(-1) for s in dense],
+                                 [buf[s.offset:s.offset + s.length] for s in dense])
 
     # ── topology synchronisation ────────────────────────────────────────
     def broadcast_topology(self, src: int = 0) -> None:
