@@ -731,6 +731,17 @@ int launch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_
 template <int VEC>
 int dispatch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_t s) {
     const int64_t nv = (N + VEC - 1) / VEC;
+    // SPARSECORE_B200_FWD_TILE=32|64|128|256: column tile of the row-gather
+    // kernel at large N (measurements; narrower tiles make the resident
+    // warps' X slice smaller, so more of its gathers hit L1).
+    if (const char* e = std::getenv("SPARSECORE_B200_FWD_TILE")) {
+        const int t = std::atoi(e);
+        if (VEC == 4 && nv >= 64) {
+            if (t == 32) return launch_fwd<VEC, 8, 1>(W, X, N, Y, s);
+            if (t == 64) return launch_fwd<VEC, 16, 1>(W, X, N, Y, s);
+            if (t == 128) return launch_fwd<VEC, 32, 1>(W, X, N, Y, s);
+        }
+    }
     if (nv >= 64) return launch_fwd<VEC, 32, 2>(W, X, N, Y, s);
     if (nv > 16) return launch_fwd<VEC, 32, 1>(W, X, N, Y, s);
     if (nv > 8) return launch_fwd<VEC, 16, 1>(W, X, N, Y, s);
