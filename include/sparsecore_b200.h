@@ -92,6 +92,14 @@ SL_API int sl_selftest_bounded_wait(int64_t spins, void* stream);
  * (sparselab/ops.py:201-203). */
 SL_API int sl_spmm_fwd(const sl_csr* W, const float* X, int64_t K, int64_t N,
                 float* Y, void* stream);
+/* Forward with the GELU of a SparseLinear -> GELU pair fused in
+ * (sparselab/nn.py:229-245 applies the activation separately): Y as
+ * sl_spmm_fwd and H[M,N] = gelu(Y) with torch's exact-erf GELU rounding
+ * ((y * 0.5) * (1 + erf(y * sqrt(1/2))), each step rounded to fp32), written
+ * by the same kernel where the X-stationary or row-gather decomposition
+ * runs, else by a second pass.  Y is kept for the GELU backward. */
+SL_API int sl_spmm_fwd_gelu(const sl_csr* W, const float* X, int64_t K, int64_t N,
+                     float* Y, float* H, void* stream);
 
 /* ── SDDMM weight gradient ────────────────────────────────────────────────
  * dW[slot] = <dY[i,:], X[col[slot],:]> for live slots of row i, 0 for

@@ -54,6 +54,14 @@ __device__ __forceinline__ void fma_vec(float v, float4 x, float* acc) {
 }
 __device__ __forceinline__ void fma_vec(float v, float x, float* acc) { acc[0] = fmaf(v, x, acc[0]); }
 
+// Exact (erf) GELU with the rounding steps of torch's CUDA kernel for
+// F.gelu(approximate="none"): (x * 0.5) * (1 + erf(x * sqrt(1/2))), each
+// operation rounded to fp32 -- so a fused epilogue matches torch bit for bit.
+__device__ __forceinline__ float gelu_erf(float x) {
+    const float kAlpha = 0.70710678118654752440f;
+    return __fmul_rn(__fmul_rn(x, 0.5f), __fadd_rn(1.0f, erff(__fmul_rn(x, kAlpha))));
+}
+
 // Slot staging.  Per chunk the warp moves slots [base, base+CH) of each of
 // its RPW rows into shared memory (row r at st + r*(CH+1)).  The loads of a
 // chunk go to registers first (ITER = RPW*CH/32 per lane, one row-run of CH
@@ -111,7 +119,7 @@ __global__ void __launch_bounds__(kFwdThreads)
 spmm_fwd_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
                 const int32_t* __restrict__ row_nnz, const int32_t* __restrict__ cols,
                 const float* __restrict__ vals, const float* __restrict__ X,
-                float* __restrict__ Y, int64_t n_tiles, int64_t n_items) {
+                float* __restrict__ Y, int64_t n_tiles, int64_t n_items, float* __restrict__ H) {
     constexpr int RPW = 32 / LPR;
     constexpr int TILE = LPR * VEC * CPL;
     constexpr int CH = ChunkOf<LPR>::value;
@@ -181,8 +189,13 @@ spmm_fwd_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
                     if constexpr (VEC == 4) {
                         *reinterpret_cast<float4*>(yr + j) =
                             make_float4(acc[cc][0], acc[cc][1], acc[cc][2], acc[cc][3]);
+                        if (H)
+                            *reinterpret_cast<float4*>(H + static_cast<int64_t>(row) * N + j) =
+                                make_float4(gelu_erf(acc[cc][0]), gelu_erf(acc[cc][1]),
+                                            gelu_erf(acc[cc][2]), gelu_erf(acc[cc][3]));
                     } else {
                         yr[j] = acc[cc][0];
+                        if (H) H[static_cast<int64_t>(row) * N + j] = gelu_erf(acc[cc][0]);
                     }
                 }
             }
@@ -707,7 +720,8 @@ int dispatch_rowwarp(const sl_csr* W, const float* X, int64_t N, float* Y, cudaS
 }
 
 template <int VEC, int LPR, int CPL>
-int launch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_t s) {
+int launch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_t s,
+               float* H = nullptr) {
     constexpr int RPW = 32 / LPR;
     constexpr int TILE = LPR * VEC * CPL;
     const int M = static_cast<int>(W->nrows);
@@ -722,14 +736,15 @@ int launch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_
     if (blocks > max_blocks) blocks = max_blocks;
     note_kernel("spmm_fwd_kernel");
     spmm_fwd_kernel<VEC, LPR, CPL><<<static_cast<unsigned>(blocks), threads, 0, s>>>(
-        M, N, W->row_start, W->row_nnz, W->col_indices, W->values, X, Y, n_tiles, n_items);
+        M, N, W->row_start, W->row_nnz, W->col_indices, W->values, X, Y, n_tiles, n_items, H);
     SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd");
     return SL_OK;
 }
 
 // Lane layout by the number of column vectors per row.
 template <int VEC>
-int dispatch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_t s) {
+int dispatch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_t s,
+                 float* H = nullptr) {
     const int64_t nv = (N + VEC - 1) / VEC;
     // SPARSECORE_B200_FWD_TILE=32|64|128|256: column tile of the row-gather
     // kernel at large N (measurements; narrower tiles make the resident
@@ -737,18 +752,18 @@ int dispatch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStrea
     if (const char* e = std::getenv("SPARSECORE_B200_FWD_TILE")) {
         const int t = std::atoi(e);
         if (VEC == 4 && nv >= 64) {
-            if (t == 32) return launch_fwd<VEC, 8, 1>(W, X, N, Y, s);
-            if (t == 64) return launch_fwd<VEC, 16, 1>(W, X, N, Y, s);
-            if (t == 128) return launch_fwd<VEC, 32, 1>(W, X, N, Y, s);
+            if (t == 32) return launch_fwd<VEC, 8, 1>(W, X, N, Y, s, H);
+            if (t == 64) return launch_fwd<VEC, 16, 1>(W, X, N, Y, s, H);
+            if (t == 128) return launch_fwd<VEC, 32, 1>(W, X, N, Y, s, H);
         }
     }
-    if (nv >= 64) return launch_fwd<VEC, 32, 2>(W, X, N, Y, s);
-    if (nv > 16) return launch_fwd<VEC, 32, 1>(W, X, N, Y, s);
-    if (nv > 8) return launch_fwd<VEC, 16, 1>(W, X, N, Y, s);
-    if (nv > 4) return launch_fwd<VEC, 8, 1>(W, X, N, Y, s);
-    if (nv > 2) return launch_fwd<VEC, 4, 1>(W, X, N, Y, s);
-    if (nv > 1) return launch_fwd<VEC, 2, 1>(W, X, N, Y, s);
-    return launch_fwd<VEC, 1, 1>(W, X, N, Y, s);
+    if (nv >= 64) return launch_fwd<VEC, 32, 2>(W, X, N, Y, s, H);
+    if (nv > 16) return launch_fwd<VEC, 32, 1>(W, X, N, Y, s, H);
+    if (nv > 8) return launch_fwd<VEC, 16, 1>(W, X, N, Y, s, H);
+    if (nv > 4) return launch_fwd<VEC, 8, 1>(W, X, N, Y, s, H);
+    if (nv > 2) return launch_fwd<VEC, 4, 1>(W, X, N, Y, s, H);
+    if (nv > 1) return launch_fwd<VEC, 2, 1>(W, X, N, Y, s, H);
+    return launch_fwd<VEC, 1, 1>(W, X, N, Y, s, H);
 }
 
 
@@ -778,7 +793,7 @@ __global__ void __launch_bounds__(xs_threads<LPR>())
 spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
                const int32_t* __restrict__ row_start, const int32_t* __restrict__ row_nnz,
                const int32_t* __restrict__ cols, const float* __restrict__ vals,
-               float* __restrict__ Y, int nbox, int row_chunks, int64_t n_items,
+               float* __restrict__ Y, float* __restrict__ H, int nbox, int row_chunks, int64_t n_items,
                int64_t items_per_cta, unsigned* status) {
     constexpr int TN = 4 * LPR;
     constexpr int RPW = 32 / LPR;
@@ -866,9 +881,14 @@ spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
                 }
                 __syncwarp();
             }
-            if (valid && j < N)
+            if (valid && j < N) {
                 *reinterpret_cast<float4*>(Y + static_cast<int64_t>(row) * N + j) =
                     make_float4(acc[0], acc[1], acc[2], acc[3]);
+                if (H)
+                    *reinterpret_cast<float4*>(H + static_cast<int64_t>(row) * N + j) =
+                        make_float4(gelu_erf(acc[0]), gelu_erf(acc[1]), gelu_erf(acc[2]),
+                                    gelu_erf(acc[3]));
+            }
         }
     }
 }
@@ -894,7 +914,8 @@ int xs_lanes_for(int64_t K) {
 }
 
 template <int LPR>
-int launch_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, cudaStream_t s) {
+int launch_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, cudaStream_t s,
+              float* H = nullptr) {
     constexpr int TN = 4 * LPR;
     constexpr int RPW = 32 / LPR;
     constexpr int kXsWarps = xs_threads<LPR>() / 32;
@@ -922,7 +943,7 @@ int launch_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, c
     grid = (n_items + per_cta - 1) / per_cta;
     note_kernel("spmm_xs_kernel");
     spmm_xs_kernel<LPR><<<static_cast<unsigned>(grid), xs_threads<LPR>(), smem, s>>>(
-        map, M, N, W->row_start, W->row_nnz, W->col_indices, W->values, Y, nbox, row_chunks,
+        map, M, N, W->row_start, W->row_nnz, W->col_indices, W->values, Y, H, nbox, row_chunks,
         n_items, per_cta, status);
     SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd (x-stationary)");
     return SL_OK;
@@ -940,7 +961,7 @@ int fwd_path() {
 
 // Returns -1 when the X-stationary path does not apply.
 int try_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, cudaStream_t s,
-           bool forced) {
+           bool forced, float* H = nullptr) {
     if (N < 256 || N % 4 != 0 || !aligned16(X) || !aligned16(Y) || K < 1 || K > INT_MAX) return -1;
     // Measured on B200 (config-4/5 shapes, N = 16384): with 64- or 128-column
     // tiles (K <= 768) the X-stationary kernel beats the row-gather kernel on
@@ -960,9 +981,9 @@ int try_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, cuda
         if (v == 64 && xs_lanes_for64(K)) tn = 64;
         if (v == 128 && xs_lanes_for128(K)) tn = 128;
     }
-    if (tn == 128) return launch_xs<32>(W, X, K, N, Y, s);
-    if (tn == 64) return launch_xs<16>(W, X, K, N, Y, s);
-    if (tn == 32) return launch_xs<8>(W, X, K, N, Y, s);
+    if (tn == 128) return launch_xs<32>(W, X, K, N, Y, s, H);
+    if (tn == 64) return launch_xs<16>(W, X, K, N, Y, s, H);
+    if (tn == 32) return launch_xs<8>(W, X, K, N, Y, s, H);
     return -1;
 }
 }  // namespace
@@ -970,28 +991,28 @@ int try_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, cuda
 
 using namespace slb;
 
-extern "C" int sl_spmm_fwd(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y,
-                           void* stream) {
-    if (int rc = check_csr(W, "sl_spmm_fwd")) return rc;
-    if (W->ncols != K)
-        return fail(SL_ERR_INVALID, "sl_spmm_fwd: shape mismatch. W has ncols=" +
-                                        std::to_string(W->ncols) + " but X has shape[0]=" +
-                                        std::to_string(K) +
-                                        ". Inner dimensions must match for matmul.");
-    if (N < 0) return fail(SL_ERR_INVALID, "sl_spmm_fwd: negative N");
-    if (W->nrows == 0 || N == 0) return SL_OK;
-    if (Y == nullptr || (K > 0 && X == nullptr))
-        return fail(SL_ERR_INVALID, "sl_spmm_fwd: NULL dense operand");
-    cudaStream_t s = as_stream(stream);
-    if (K == 0) return cuda_status(cudaMemsetAsync(Y, 0, sizeof(float) * W->nrows * N, s),
-                                   "sl_spmm_fwd memset");
+namespace slb {
+namespace {
+__global__ void __launch_bounds__(256) gelu_kernel(const float* __restrict__ Y, float* __restrict__ H,
+                                                   int64_t n) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        H[i] = gelu_erf(Y[i]);
+}
+
+// The forward dispatch; with H != nullptr also H = gelu(Y), fused into the
+// epilogue of the X-stationary and row-gather kernels, else a second pass.
+int spmm_fwd_impl(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, float* H,
+                  cudaStream_t s) {
     const int path = fwd_path();
-    if (path != kPathRows) {
-        const int rc = try_xs(W, X, K, N, Y, s, path == kPathXs);
-        if (rc >= 0) return rc;
+    int rc = -1;
+    if (path != kPathRows) rc = try_xs(W, X, K, N, Y, s, path == kPathXs, H);
+    if (rc >= 0) return rc;
+    if (N >= 128) {
+        const bool vec4 = (N % 4 == 0) && aligned16(X) && aligned16(Y) && (H == nullptr || aligned16(H));
+        return vec4 ? dispatch_fwd<4>(W, X, N, Y, s, H) : dispatch_fwd<1>(W, X, N, Y, s, H);
     }
     if (N == 1 && spmv_lane_enabled(W)) {
-        // SPARSECORE_B200_N1=lane keeps the cp.async lane kernel (tests).
         // Measured on B200 (4096 and 16384 rows x 4096, 50-99%): the
         // warp-specialised window kernel wins with long rows (with one CTA
         // per SM from about 100 slots per row, with more rows from about
@@ -1002,23 +1023,65 @@ extern "C" int sl_spmm_fwd(const sl_csr* W, const float* X, int64_t K, int64_t N
         bool ws = (W->nrows + 31) / 32 <= num_sms() ? avg >= 96.0 : avg >= 600.0;
         if (e != nullptr && e[0] == 'l') ws = false;
         if (e != nullptr && e[0] == 'w' && e[1] == 's') ws = true;
-        int rc = ws ? launch_spmv_ws(W, X, K, Y, s) : -1;
+        rc = ws ? launch_spmv_ws(W, X, K, Y, s) : -1;
         if (rc < 0) rc = launch_spmv(W, X, K, Y, s);
-        if (rc >= 0) return rc;
     }
-    if (N == 4 || N == 8) {
-        const int rc = try_lanerow(W, X, N, Y, s);
-        if (rc >= 0) return rc;
-    }
+    if (rc < 0 && (N == 4 || N == 8)) rc = try_lanerow(W, X, N, Y, s);
     // N = 32: the row-warp kernel (32-bit offsets) measured faster than the
     // cp.async-staged gather (4096^2 at 90%: 27.3 vs 31.9 us; L1 hits on the
     // gathered X rows, which cp.async.cg bypasses); SPARSECORE_B200_N32=gather
     // selects the staged kernel (tests).
-    if (N == 32 && gather32_forced()) {
-        const int rc = launch_gather32_fwd(W, X, Y, s);
-        if (rc >= 0) return rc;
+    if (rc < 0 && N == 32 && gather32_forced()) rc = launch_gather32_fwd(W, X, Y, s);
+    if (rc < 0) rc = dispatch_rowwarp(W, X, N, Y, s);
+    if (rc == SL_OK && H != nullptr) {
+        const int64_t n = W->nrows * N;
+        int64_t blocks = (n + 255) / 256;
+        const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
+        gelu_kernel<<<static_cast<unsigned>(blocks < cap ? blocks : cap), 256, 0, s>>>(Y, H, n);
+        SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd_gelu");
     }
-    if (N < 128) return dispatch_rowwarp(W, X, N, Y, s);
-    const bool vec4 = (N % 4 == 0) && aligned16(X) && aligned16(Y);
-    return vec4 ? dispatch_fwd<4>(W, X, N, Y, s) : dispatch_fwd<1>(W, X, N, Y, s);
+    return rc;
+}
+
+int check_fwd_args(const sl_csr* W, const float* X, int64_t K, int64_t N, const float* Y,
+                   const char* fn) {
+    if (int rc = check_csr(W, fn)) return rc;
+    if (W->ncols != K)
+        return fail(SL_ERR_INVALID, std::string(fn) + ": shape mismatch. W has ncols=" +
+                                        std::to_string(W->ncols) + " but X has shape[0]=" +
+                                        std::to_string(K) +
+                                        ". Inner dimensions must match for matmul.");
+    if (N < 0) return fail(SL_ERR_INVALID, std::string(fn) + ": negative N");
+    if (W->nrows == 0 || N == 0) return -1;  // nothing to do
+    if (Y == nullptr || (K > 0 && X == nullptr))
+        return fail(SL_ERR_INVALID, std::string(fn) + ": NULL dense operand");
+    return SL_OK;
+}
+}  // namespace
+}  // namespace slb
+
+extern "C" int sl_spmm_fwd(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y,
+                           void* stream) {
+    const int rc = check_fwd_args(W, X, K, N, Y, "sl_spmm_fwd");
+    if (rc < 0) return SL_OK;
+    if (rc != SL_OK) return rc;
+    cudaStream_t s = as_stream(stream);
+    if (K == 0) return cuda_status(cudaMemsetAsync(Y, 0, sizeof(float) * W->nrows * N, s),
+                                   "sl_spmm_fwd memset");
+    return spmm_fwd_impl(W, X, K, N, Y, nullptr, s);
+}
+
+extern "C" int sl_spmm_fwd_gelu(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y,
+                                float* H, void* stream) {
+    const int rc = check_fwd_args(W, X, K, N, Y, "sl_spmm_fwd_gelu");
+    if (rc < 0) return SL_OK;
+    if (rc != SL_OK) return rc;
+    if (H == nullptr) return fail(SL_ERR_INVALID, "sl_spmm_fwd_gelu: NULL H");
+    cudaStream_t s = as_stream(stream);
+    if (K == 0) {
+        if (int e = cuda_status(cudaMemsetAsync(Y, 0, sizeof(float) * W->nrows * N, s), "sl_spmm_fwd_gelu memset"))
+            return e;
+        return cuda_status(cudaMemsetAsync(H, 0, sizeof(float) * W->nrows * N, s), "sl_spmm_fwd_gelu memset");
+    }
+    return spmm_fwd_impl(W, X, K, N, Y, H, s);
 }

@@ -112,6 +112,20 @@ def _spmm_raw(W: PaddedCSR, X: torch.Tensor, kind: str = "spmm_fwd") -> torch.Te
     return Y
 
 
+def _spmm_gelu_raw(W: PaddedCSR, X: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(Y, gelu(Y)) with Y = W.X; the GELU fused into the forward kernel's
+    epilogue where the decomposition allows (``sl_spmm_fwd_gelu``)."""
+    M = W.nrows
+    K, Ncol = X.shape
+    Y = torch.empty(M, Ncol, dtype=torch.float32, device=X.device)
+    H = torch.empty_like(Y)
+    nnz = W.nnz
+    _launch("spmm_fwd", 8 * nnz + 8 * M + 4 * K * Ncol + 8 * M * Ncol, 2 * nnz * Ncol,
+            lambda: N.call("sl_spmm_fwd_gelu", W._abi_ref(), N.ptr(X), K, Ncol, N.ptr(Y), N.ptr(H),
+                           W._stream()))
+    return Y, H
+
+
 def _sddmm_raw(W: PaddedCSR, dY: torch.Tensor, X: torch.Tensor) -> torch.Tensor:
     """dW[total_capacity] at live slots (padding 0)."""
     dW = torch.empty(W.total_capacity, dtype=torch.float32, device=dY.device)
@@ -336,8 +350,11 @@ class _SparseMLPFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, v1, v2, x, W1, W2, act):
         X = _transpose(x)
-        Y1 = _spmm_raw(W1, X)
-        H = torch.nn.functional.gelu(Y1) if act == "gelu" else torch.relu(Y1)
+        if act == "gelu":
+            Y1, H = _spmm_gelu_raw(W1, X)  # GELU in the forward kernel's epilogue
+        else:
+            Y1 = _spmm_raw(W1, X)
+            H = torch.relu(Y1)
         Y2 = _spmm_raw(W2, H)
         ctx.save_for_backward(X, Y1, H)
         ctx.W1, ctx.W2, ctx.act = W1, W2, act

@@ -54,3 +54,22 @@ def test_sparse_mlp_falls_back_with_bias_or_hooks():
     assert torch.equal(sl.sparse_mlp(x, fc1, fc2, "relu"), fc2(torch.relu(fc1(x))))
     with pytest.raises(ValueError):
         sl.sparse_mlp(x, fc1, fc2, "tanh")
+
+
+@pytest.mark.parametrize("N,path", [(1, None), (8, None), (32, None), (185, None), (256, "rows"),
+                                    (1024, "xs"), (1024, None)])
+def test_fused_gelu_epilogue_equals_torch_gelu(N, path, monkeypatch):
+    """sl_spmm_fwd_gelu: Y equals sl_spmm_fwd's and H equals torch's exact
+    GELU of Y bit for bit, on the fused epilogues (row-gather, X-stationary)
+    and the second-pass kernel (small N); values span the GELU's range."""
+    import sparsecore_b200 as sl
+    from sparsecore_b200 import ops
+
+    if path is not None:
+        monkeypatch.setenv("SPARSECORE_B200_FWD", path)
+    g = torch.Generator().manual_seed(N)
+    W = sl.PaddedCSR.random(300, 700, sparsity=0.8, seed=N)
+    X = (torch.randn(700, N, generator=g) * 3.0).to(dev())
+    Y, H = ops._spmm_gelu_raw(W, X)
+    assert bits_equal(Y, ops._spmm_raw(W, X))
+    assert bits_equal(H, torch.nn.functional.gelu(Y))
