@@ -286,6 +286,7 @@ __device__ __forceinline__ int consumer_exclusive_scan(int v, int* ws, int* tota
     return base + inc - v;
 }
 
+template <bool SEG>
 __global__ void __launch_bounds__(kTThreads + 32, 2)
 sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_constant__ CUtensorMap xmap,
                    int M, int64_t N, int TR, int TC, int n_bc, int n_bi, int col_major, int shared_first,
@@ -301,6 +302,7 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
     __shared__ int ws[(kTThreads + 32) / 32];
     __shared__ int ord_slot[kTBatch];  // batch position -> global slot (-1 = none)
     __shared__ int ord_rc[kTBatch];    // (tile row << 16) | tile column
+    __shared__ int seg_pref[kTMaxRows + 1];  // SEG: exclusive scan of ceil(run / 8)
 
     const int tid = threadIdx.x, lane = tid & 31, q = lane & 3, quad = tid >> 2;
     const bool producer = tid >= kTThreads;  // warp 8 issues the copies
@@ -325,6 +327,12 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
     const int ex = block_exclusive_scan<kTThreads + 32>(cnt, ws, &total);
     if (tid < TR) run_pref[tid] = ex;
     if (tid == 0) run_pref[TR] = total;
+    int nseg = 0;  // SEG: segments of up to kTS slots of one row, the batching unit
+    if constexpr (SEG) {
+        const int sx = block_exclusive_scan<kTThreads + 32>((cnt + kTS - 1) / kTS, ws, &nseg);
+        if (tid < TR) seg_pref[tid] = sx;
+        if (tid == 0) seg_pref[TR] = nseg;
+    }
     if (bc == 0) {  // padding slots of the tile's rows -> 0
         for (int r = tid >> 5; r < nrows; r += (kTThreads + 32) / 32) {
             const int rs = __ldg(row_start + r0 + r);
@@ -345,7 +353,7 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
     // Stage b: dY block at sbase + b*stage, X block right after it.
     const int stage = (TR + TC) * kTJ;
     const int nchunks = static_cast<int>(N / kTJ);
-    const int nbatch = (total + kTBatch - 1) / kTBatch;
+    const int nbatch = SEG ? (nseg + kTQuads - 1) / kTQuads : (total + kTBatch - 1) / kTBatch;
     const int nsteps = nbatch * nchunks;  // step g = batch * nchunks + chunk
 
     if (producer) {
@@ -384,6 +392,92 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
     // but still reaches every named barrier, so no consumer is left waiting.
     bool ok = true;
     unsigned fph = 0u;  // bit b = parity of stage b's next fill
+    if constexpr (SEG) {
+        // Segmented batches: quad Q takes segment g = bt * 64 + Q, i.e. up
+        // to kTS consecutive live slots of ONE tile row, so the quad loads
+        // that row's dY chunk once per chunk instead of at every row change
+        // inside its slots.  Within the segment the slots are ordered by the
+        // bank half of their X row -- even quads take class 0 first, odd
+        // quads class 1 first -- so the two quads of a quarter-warp mostly
+        // read opposite bank halves.  Each slot is its own dot product, so
+        // the order of a quad's slots does not touch the rounding.
+        for (int bt = 0; bt < nbatch; ++bt) {
+            const int g = bt * kTQuads + quad;
+            int r = 0, ns = 0, base = 0;
+            if (g < nseg) {
+                int lo = 0, hi = TR;  // last r with seg_pref[r] <= g
+                while (hi - lo > 1) {
+                    const int mid = (lo + hi) >> 1;
+                    if (seg_pref[mid] <= g) lo = mid; else hi = mid;
+                }
+                r = lo;
+                const int j0 = kTS * (g - seg_pref[r]);
+                ns = min(kTS, run_pref[r + 1] - run_pref[r] - j0);
+                base = run_lo[r] + j0;
+            }
+            int cl[kTS];
+            unsigned cls = 0u;
+#pragma unroll
+            for (int t = 0; t < kTS; ++t) {
+                cl[t] = t < ns ? __ldg(cols + base + t) - c0 : 0;
+                if ((cl[t] >> 2) & 1) cls |= 1u << t;
+            }
+            const unsigned want = (quad & 1) ? 1u : 0u;  // class taken first
+            int off[kTS], sid[kTS], key[kTS];
+#pragma unroll
+            for (int t = 0; t < kTS; ++t) {
+                off[t] = TR * kTJ + cl[t] * kTJ + ((q ^ (cl[t] & 7)) << 2);
+                sid[t] = base + t;
+                key[t] = t < ns ? (((cls >> t) & 1u) == want ? 0 : 1) : 2;
+            }
+            // Batcher's odd-even merge sort of the 8 (key, off, sid) triples
+            // by key: fixed compare-exchanges keep the arrays in registers.
+            constexpr int kNet[19][2] = {{0, 1}, {2, 3}, {4, 5}, {6, 7}, {0, 2}, {1, 3}, {4, 6},
+                                         {5, 7}, {1, 2}, {5, 6}, {0, 4}, {1, 5}, {2, 6}, {3, 7},
+                                         {2, 4}, {3, 5}, {1, 2}, {3, 4}, {5, 6}};
+#pragma unroll
+            for (int e = 0; e < 19; ++e) {
+                const int a = kNet[e][0], b = kNet[e][1];
+                const bool sw = key[b] < key[a];
+                const int ka = sw ? key[b] : key[a], kb = sw ? key[a] : key[b];
+                const int oa = sw ? off[b] : off[a], ob = sw ? off[a] : off[b];
+                const int ia = sw ? sid[b] : sid[a], ib = sw ? sid[a] : sid[b];
+                key[a] = ka; key[b] = kb; off[a] = oa; off[b] = ob; sid[a] = ia; sid[b] = ib;
+            }
+            const int yo = r * kTJ + ((q ^ (r & 7)) << 2);
+            float4 acc[kTS];
+#pragma unroll
+            for (int t = 0; t < kTS; ++t) acc[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int kc = 0; kc < nchunks; ++kc) {
+                const int b = (bt * nchunks + kc) % kTStages;
+                if (ok && !mbar_wait(&full[b], (fph >> b) & 1u, status)) ok = false;  // bounded
+                fph ^= 1u << b;
+                const float* sb = sbase + b * stage;
+                const float4 d0 = *reinterpret_cast<const float4*>(sb + yo);
+                const float4 d1 = *reinterpret_cast<const float4*>(sb + (yo ^ 16));
+#pragma unroll
+                for (int t = 0; t < kTS; ++t) {
+                    if (t < ns) {
+                        fma4(d0, *reinterpret_cast<const float4*>(sb + off[t]), acc[t]);
+                        fma4(d1, *reinterpret_cast<const float4*>(sb + (off[t] ^ 16)), acc[t]);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[b]);  // this warp is done with stage b
+            }
+#pragma unroll
+            for (int t = 0; t < kTS; ++t) {
+                const float4 o = shfl_xor4(acc[t], 2);
+                if (q < 2) acc[t] = add4(acc[t], o);
+                const float4 hi = shfl_xor4(acc[t], 1);
+                if (q == 0 && ok && t < ns) {
+                    const float4 s4 = add4(acc[t], hi);
+                    dW[sid[t]] = __fadd_rn(__fadd_rn(s4.x, s4.z), __fadd_rn(s4.y, s4.w));
+                }
+            }
+        }
+        return;
+    }
     for (int bt = 0; bt < nbatch; ++bt) {
         // Batch order.  A warp-wide 128-bit shared load is served one
         // quarter-warp (two quads) at a time, and a quad reads one 64-byte
@@ -566,7 +660,12 @@ int try_tiled(const sl_csr* W, const float* dY, const float* X, int64_t N, float
         const int v = std::atoi(e);
         if (v == 64 || v == 128 || v == 256) TC = v;
     }
-    int TR = static_cast<int>(std::floor(480.0 / (TC * dens) / 8.0)) * 8;
+    // Segmented batches (default; SPARSECORE_B200_DW_SEG=0 keeps the slot
+    // batches): about 60 of the 64 quads' segments per tile.
+    bool seg = true;
+    if (const char* e = std::getenv("SPARSECORE_B200_DW_SEG")) seg = e[0] != '0';
+    int TR = seg ? static_cast<int>(std::floor(60.0 / (TC * dens / kTS + 0.55) / 8.0)) * 8
+                 : static_cast<int>(std::floor(480.0 / (TC * dens) / 8.0)) * 8;
     TR = TR < 8 ? 8 : (TR > kTMaxRows ? kTMaxRows : TR);
     unsigned* status = device_status_word();
     if (status == nullptr) return -1;
@@ -574,7 +673,7 @@ int try_tiled(const sl_csr* W, const float* dY, const float* X, int64_t N, float
     if (!make_tmap_2d(&dymap, dY, M, N, TR, kTJ, true) || !make_tmap_2d(&xmap, X, K, N, TC, kTJ, true))
         return -1;
     const size_t smem = static_cast<size_t>(kTStages * (TR + TC) * kTJ * 4) + 1024;
-    auto kern = sddmm_tiled_kernel;
+    auto kern = seg ? sddmm_tiled_kernel<true> : sddmm_tiled_kernel<false>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
         return -1;

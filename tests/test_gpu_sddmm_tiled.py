@@ -70,16 +70,19 @@ def test_tiled_sddmm_config5_ffn_up_at_training_width():
     assert bits_equal(y, O.spmm(Wo, X.numpy()))
 
 
+@pytest.mark.parametrize("seg", ["1", "0"])
 @pytest.mark.parametrize("tc", ["64", "128", "256"])
 @pytest.mark.parametrize("order", ["row", "col"])
-def test_tiled_sddmm_tile_widths_and_orders(tc, order, monkeypatch):
-    """Every tile width and both tile orders, on ragged edges (M, K not
-    multiples of any tile) with a dense block that puts thousands of slots in
-    one tile (several 512-slot batches per tile)."""
+def test_tiled_sddmm_tile_widths_and_orders(tc, order, seg, monkeypatch):
+    """Every tile width and both tile orders, with segmented (default) and
+    slot batches, on ragged edges (M, K not multiples of any tile) with a
+    dense block that puts thousands of slots in one tile (several batches
+    per tile)."""
     from oracle import oracle as O
 
     W, X, dY = _case(1000, 1100, 0.06, 1024, seed=17, block=(130, 300))
     ref = O.sddmm(oracle_csr(W), dY.numpy(), X.numpy())
+    monkeypatch.setenv("SPARSECORE_B200_DW_SEG", seg)
     monkeypatch.setenv("SPARSECORE_B200_DW_TC", tc)
     monkeypatch.setenv("SPARSECORE_B200_DW_ORDER", order)
     assert bits_equal(_dw_checked(W, dY.to(dev()), X.to(dev())), ref)
