@@ -25,6 +25,9 @@
 //    (segments of 128 slots, 4 per lane).
 #include <cmath>
 #include <cstdlib>
+#include <functional>
+#include <map>
+#include <mutex>
 
 #include "common.cuh"
 #include "tma.cuh"
@@ -643,27 +646,19 @@ int launch_dw_n1(const sl_csr* W, const float* dY, const float* X, float* dW, cu
     return SL_OK;
 }
 
-// Returns -1 when the tiled path does not apply.
-int try_tiled(const sl_csr* W, const float* dY, const float* X, int64_t N, float* dW, cudaStream_t s) {
+// One launch of the tiled kernel, slot batches (seg = false) or segmented
+// batches (seg = true).  Returns -1 when it cannot be configured.
+int launch_tiled(const sl_csr* W, const float* dY, const float* X, int64_t N, float* dW,
+                 cudaStream_t s, double dens, bool seg) {
     const int64_t M = W->nrows, K = W->ncols;
-    if (N < 1024 || N % kTJ != 0 || !aligned16(dY) || !aligned16(X) || N > INT_MAX / 2) return -1;
-    // Live density estimate from the capacity (live + about 20% padding).
-    // Measured on B200 (standalone sweep): the tiled kernel wins for
-    // 2% <= density <= 40% once N >= 1024; at N = 256 its pipeline barely
-    // fills, and at 50% density its tiles shrink to 8 rows.
-    const double dens = static_cast<double>(W->total_capacity) / 1.2 / (static_cast<double>(M) * K);
-    if (dens < 0.02 || dens > 0.4) return -1;
-    // Wide tiles at low density (more slots per tile row: fewer dY reloads),
-    // about 480 slots per tile (the batch holds 512).
+    // Wide tiles at low density (more slots per tile row: fewer dY reloads).
     int TC = dens <= 0.15 ? 128 : 64;
     if (const char* e = std::getenv("SPARSECORE_B200_DW_TC")) {  // tuning knob: 64|128|256
         const int v = std::atoi(e);
         if (v == 64 || v == 128 || v == 256) TC = v;
     }
-    // Segmented batches (default; SPARSECORE_B200_DW_SEG=0 keeps the slot
-    // batches): about 60 of the 64 quads' segments per tile.
-    bool seg = true;
-    if (const char* e = std::getenv("SPARSECORE_B200_DW_SEG")) seg = e[0] != '0';
+    // Slot batches: about 480 slots per tile (the batch holds 512).
+    // Segmented batches: about 60 of the 64 quads' segments per tile.
     int TR = seg ? static_cast<int>(std::floor(60.0 / (TC * dens / kTS + 0.55) / 8.0)) * 8
                  : static_cast<int>(std::floor(480.0 / (TC * dens) / 8.0)) * 8;
     TR = TR < 8 ? 8 : (TR > kTMaxRows ? kTMaxRows : TR);
@@ -695,6 +690,80 @@ int try_tiled(const sl_csr* W, const float* dY, const float* X, int64_t N, float
         W->row_nnz, W->row_capacity, W->col_indices, dW, status);
     SL_RETURN_IF_LAUNCH_FAILED("sl_sddmm_dw (tiled)");
     return SL_OK;
+}
+
+// Batch form per problem shape, chosen by timing both on the shape's first
+// call (outside stream capture; both are bit-identical, so the choice never
+// changes a value) and cached for the process.  Measured on B200 at N =
+// 16384: segmented batches win on config-5 o (7.7 vs 6.5 TFLOP/s) and
+// config-4 qkv (7.0 vs 5.5), slot batches on the other config-4/5 layers
+// (e.g. ffn_up 7.6 vs 6.9).  SPARSECORE_B200_DW_SEG=0|1 forces one.
+struct DwKey {
+    int64_t M, K, cap, N;
+    bool operator<(const DwKey& o) const {
+        if (M != o.M) return M < o.M;
+        if (K != o.K) return K < o.K;
+        if (cap != o.cap) return cap < o.cap;
+        return N < o.N;
+    }
+};
+std::mutex g_dw_mu;
+std::map<std::pair<int, DwKey>, bool> g_dw_seg;  // (device, shape) -> segmented
+
+float time_launch_ms(cudaStream_t s, const std::function<int()>& fn, int* rc) {
+    cudaEvent_t a, b;
+    if (cudaEventCreate(&a) != cudaSuccess) return -1.0f;
+    if (cudaEventCreate(&b) != cudaSuccess) { cudaEventDestroy(a); return -1.0f; }
+    cudaEventRecord(a, s);
+    *rc = fn();
+    cudaEventRecord(b, s);
+    float ms = -1.0f;
+    if (*rc == SL_OK && cudaEventSynchronize(b) == cudaSuccess) cudaEventElapsedTime(&ms, a, b);
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    return ms;
+}
+
+// Returns -1 when the tiled path does not apply.
+int try_tiled(const sl_csr* W, const float* dY, const float* X, int64_t N, float* dW, cudaStream_t s) {
+    const int64_t M = W->nrows, K = W->ncols;
+    if (N < 1024 || N % kTJ != 0 || !aligned16(dY) || !aligned16(X) || N > INT_MAX / 2) return -1;
+    // Live density estimate from the capacity (live + about 20% padding).
+    // Measured on B200 (standalone sweep): the tiled kernel wins for
+    // 2% <= density <= 40% once N >= 1024; at N = 256 its pipeline barely
+    // fills, and at 50% density its tiles shrink to 8 rows.
+    const double dens = static_cast<double>(W->total_capacity) / 1.2 / (static_cast<double>(M) * K);
+    if (dens < 0.02 || dens > 0.4) return -1;
+    if (const char* e = std::getenv("SPARSECORE_B200_DW_SEG"))
+        return launch_tiled(W, dY, X, N, dW, s, dens, e[0] != '0');
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const std::pair<int, DwKey> key{dev, DwKey{M, K, W->total_capacity, N}};
+    {
+        std::lock_guard<std::mutex> lock(g_dw_mu);
+        auto it = g_dw_seg.find(key);
+        if (it != g_dw_seg.end()) return launch_tiled(W, dY, X, N, dW, s, dens, it->second);
+    }
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone)
+        return launch_tiled(W, dY, X, N, dW, s, dens, false);  // cannot time under capture
+    // Warm both (module load, attributes), then time one launch of each.
+    int rc_a = launch_tiled(W, dY, X, N, dW, s, dens, false);
+    if (rc_a != SL_OK) return rc_a;
+    int rc_b = launch_tiled(W, dY, X, N, dW, s, dens, true);
+    const bool seg_ok = rc_b == SL_OK;
+    float ms_a = time_launch_ms(s, [&] { return launch_tiled(W, dY, X, N, dW, s, dens, false); }, &rc_a);
+    if (rc_a != SL_OK) return rc_a;
+    float ms_b = -1.0f;
+    if (seg_ok) ms_b = time_launch_ms(s, [&] { return launch_tiled(W, dY, X, N, dW, s, dens, true); }, &rc_b);
+    const bool seg = seg_ok && rc_b == SL_OK && ms_a > 0.0f && ms_b > 0.0f && ms_b < ms_a;
+    {
+        std::lock_guard<std::mutex> lock(g_dw_mu);
+        g_dw_seg[key] = seg;
+    }
+    // The last launch left the same dW as either form would; finish with the
+    // chosen one so sl_last_kernel and the output are those of the choice.
+    return launch_tiled(W, dY, X, N, dW, s, dens, seg);
 }
 
 // SPARSECORE_B200_DW=quad forces the per-slot kernels (tuning and tests).
