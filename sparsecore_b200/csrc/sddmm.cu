@@ -692,12 +692,15 @@ int launch_tiled(const sl_csr* W, const float* dY, const float* X, int64_t N, fl
     return SL_OK;
 }
 
-// Batch form per problem shape, chosen by timing both on the shape's first
-// call (outside stream capture; both are bit-identical, so the choice never
-// changes a value) and cached for the process.  Measured on B200 at N =
-// 16384: segmented batches win on config-5 o (7.7 vs 6.5 TFLOP/s) and
-// config-4 qkv (7.0 vs 5.5), slot batches on the other config-4/5 layers
-// (e.g. ffn_up 7.6 vs 6.9).  SPARSECORE_B200_DW_SEG=0|1 forces one.
+// Batch form: slot batches by default.  SPARSECORE_B200_DW_SEG=1 forces the
+// segmented form, =auto picks per problem shape by timing both on the
+// shape's first call (outside stream capture; both are bit-identical, so
+// the choice never changes a value) and caches it.  Measured on B200 at N =
+// 16384: timed alone, segmented batches win on config-5 o (7.7 vs 6.5
+// TFLOP/s) and config-4 qkv (7.0 vs 5.5) and lose on the other config-4/5
+// layers (e.g. ffn_up 6.9 vs 7.6); but in the config-5 training step, where
+// the SDDMM runs beside dX on a side stream, the per-shape choice made the
+// step slower (110.8 vs 109.8 ms), so it is not the default.
 struct DwKey {
     int64_t M, K, cap, N;
     bool operator<(const DwKey& o) const {
@@ -734,8 +737,9 @@ int try_tiled(const sl_csr* W, const float* dY, const float* X, int64_t N, float
     // fills, and at 50% density its tiles shrink to 8 rows.
     const double dens = static_cast<double>(W->total_capacity) / 1.2 / (static_cast<double>(M) * K);
     if (dens < 0.02 || dens > 0.4) return -1;
-    if (const char* e = std::getenv("SPARSECORE_B200_DW_SEG"))
-        return launch_tiled(W, dY, X, N, dW, s, dens, e[0] != '0');
+    const char* mode = std::getenv("SPARSECORE_B200_DW_SEG");
+    if (mode == nullptr || mode[0] != 'a')
+        return launch_tiled(W, dY, X, N, dW, s, dens, mode != nullptr && mode[0] == '1');
     int dev = 0;
     cudaGetDevice(&dev);
     const std::pair<int, DwKey> key{dev, DwKey{M, K, W->total_capacity, N}};

@@ -70,12 +70,12 @@ def test_tiled_sddmm_config5_ffn_up_at_training_width():
     assert bits_equal(y, O.spmm(Wo, X.numpy()))
 
 
-@pytest.mark.parametrize("seg", ["1", "0"])
+@pytest.mark.parametrize("seg", ["1", "0", "auto"])
 @pytest.mark.parametrize("tc", ["64", "128", "256"])
 @pytest.mark.parametrize("order", ["row", "col"])
 def test_tiled_sddmm_tile_widths_and_orders(tc, order, seg, monkeypatch):
-    """Every tile width and both tile orders, with segmented (default) and
-    slot batches, on ragged edges (M, K not multiples of any tile) with a
+    """Every tile width and both tile orders, with slot (default) and
+    segmented batches and the per-shape timed choice, on ragged edges (M, K not multiples of any tile) with a
     dense block that puts thousands of slots in one tile (several batches
     per tile)."""
     from oracle import oracle as O
