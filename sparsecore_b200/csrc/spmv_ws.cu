@@ -59,13 +59,15 @@ __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0
 // single-warp version of the same windows, 1.2-1.9x slower with few rows,
 // and 1-D bulk copies of each row's window instead of cp.async, up to 1.9x
 // slower.)
-template <int WIN>
+template <int WIN, int RPC = 32>
 struct WsShape {
     static constexpr int kStride = WIN + 4;                 // words per row slice
-    static constexpr int kStageWords = 32 * kStride;        // one array, one stage
+    static constexpr int kStageWords = RPC * kStride;       // one array, one stage
 };
 
-template <int WIN, int S, bool KS>
+// RPC = rows per CTA: 32, or 16 (lanes 16-31 idle) so that with few rows
+// twice as many CTAs -- and copies in flight -- share the SMs.
+template <int WIN, int S, bool KS, int RPC = 32>
 __global__ void __launch_bounds__(96, 1)
 spmv_ws_kernel(int M, int64_t K, int64_t cap_total, const int32_t* __restrict__ row_start,
                const int32_t* __restrict__ row_nnz, const int32_t* __restrict__ cols,
@@ -74,7 +76,7 @@ spmv_ws_kernel(int M, int64_t K, int64_t cap_total, const int32_t* __restrict__ 
     static_assert(S % 2 == 0 && S >= 4, "two producers, at least two stages each");
     constexpr int D = S / 2;
     constexpr int kStr = WsShape<WIN>::kStride;
-    constexpr int kSW = WsShape<WIN>::kStageWords;
+    constexpr int kSW = WsShape<WIN, RPC>::kStageWords;
     constexpr size_t kRing = size_t(S) * kSW * 4 * 2;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t full[S];
@@ -85,8 +87,8 @@ spmv_ws_kernel(int M, int64_t K, int64_t cap_total, const int32_t* __restrict__ 
     float* xs = reinterpret_cast<float*>(smem_raw + kRing + 16);
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int row = blockIdx.x * 32 + lane;
-    const bool live = row < M;
+    const int row = blockIdx.x * RPC + lane;
+    const bool live = lane < RPC && row < M;
     const int rs = live ? __ldg(row_start + row) : 0;
     const int nn = live ? __ldg(row_nnz + row) : 0;
     const int a = rs & ~3;
@@ -158,7 +160,7 @@ spmv_ws_kernel(int M, int64_t K, int64_t cap_total, const int32_t* __restrict__ 
         int* cdst = cring + b * kSW + sub * kStr + 4 * li;
         float* vdst = vring + b * kSW + sub * kStr + 4 * li;
 #pragma unroll 4
-        for (int rr = 0; rr < 32; rr += RPI) {
+        for (int rr = 0; rr < RPC; rr += RPI) {
             const int r = rr + sub;
             const int ra = __shfl_sync(0xffffffffu, a, r);
             const int re = __shfl_sync(0xffffffffu, ecopy, r);
@@ -232,22 +234,27 @@ spmv_ws_kernel(int M, int64_t K, int64_t cap_total, const int32_t* __restrict__ 
     cp_wait<0>();
 }
 
-template <int WIN, int S, bool KS>
+template <int WIN, int S, bool KS, int RPC>
 int launch_ws(const sl_csr* W, const float* X, int64_t K, float* Y, cudaStream_t s) {
     unsigned* status = device_status_word();
     if (status == nullptr) return -1;
-    const size_t smem = size_t(S) * WsShape<WIN>::kStageWords * 4 * 2 + 16 +
+    const size_t smem = size_t(S) * WsShape<WIN, RPC>::kStageWords * 4 * 2 + 16 +
                         (KS ? static_cast<size_t>(K) * 4 : 0);
-    auto kern = spmv_ws_kernel<WIN, S, KS>;
+    auto kern = spmv_ws_kernel<WIN, S, KS, RPC>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
         return -1;
     const int M = static_cast<int>(W->nrows);
     note_kernel("spmv_ws_kernel");
-    kern<<<(M + 31) / 32, 96, smem, s>>>(M, K, W->total_capacity, W->row_start, W->row_nnz,
-                                         W->col_indices, W->values, X, Y, status);
+    kern<<<(M + RPC - 1) / RPC, 96, smem, s>>>(M, K, W->total_capacity, W->row_start, W->row_nnz,
+                                               W->col_indices, W->values, X, Y, status);
     SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd (N = 1, warp-specialised)");
     return SL_OK;
+}
+
+template <int S, int RPC>
+int launch_ws_x(const sl_csr* W, const float* X, int64_t K, float* Y, cudaStream_t s, bool ks) {
+    return ks ? launch_ws<64, S, true, RPC>(W, X, K, Y, s) : launch_ws<64, S, false, RPC>(W, X, K, Y, s);
 }
 
 }  // namespace
@@ -272,8 +279,12 @@ int launch_spmv_ws(const sl_csr* W, const float* X, int64_t K, float* Y, cudaStr
     const double row_bytes = 8.0 * static_cast<double>(W->total_capacity) / 1.2 / W->nrows;
     bool ks = K <= kMaxKs && 4.0 * K <= 0.5 * 32.0 * row_bytes;
     if (const char* e = std::getenv("SPARSECORE_B200_N1_XS")) ks = (e[0] == '1') && K <= kMaxKs;
-    if (st == 8) return ks ? launch_ws<64, 8, true>(W, X, K, Y, s) : launch_ws<64, 8, false>(W, X, K, Y, s);
-    return ks ? launch_ws<64, 4, true>(W, X, K, Y, s) : launch_ws<64, 4, false>(W, X, K, Y, s);
+    // Rows per CTA: 16 when 32-row CTAs would not give every SM one (more
+    // CTAs, and copies in flight, per SM); SPARSECORE_B200_N1_RPC=16|32.
+    int rpc = warps <= num_sms() ? 16 : 32;
+    if (const char* e = std::getenv("SPARSECORE_B200_N1_RPC")) rpc = std::atoi(e) == 16 ? 16 : 32;
+    if (rpc == 16) return st == 8 ? launch_ws_x<8, 16>(W, X, K, Y, s, ks) : launch_ws_x<4, 16>(W, X, K, Y, s, ks);
+    return st == 8 ? launch_ws_x<8, 32>(W, X, K, Y, s, ks) : launch_ws_x<4, 32>(W, X, K, Y, s, ks);
 }
 
 }  // namespace slb

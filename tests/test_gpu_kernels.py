@@ -270,9 +270,12 @@ def test_spmv_lane_kernel_matches_oracle_and_warp_kernel(M, K, s, pr, monkeypatc
     for xs in ("1", "0"):  # X in shared memory / through L1
         monkeypatch.setenv("SPARSECORE_B200_N1_XS", xs)
         for st in ("4", "8"):  # both ring depths
-            monkeypatch.setenv("SPARSECORE_B200_N1_ST", st)
-            assert bits_equal(sl.spmm(W, X.to(d)), y), (xs, st)
-            assert bits_equal(ops._spmm_raw(WT, dY.to(d)), dx), (xs, st)
+            for rpc in ("16", "32"):  # rows per CTA
+                monkeypatch.setenv("SPARSECORE_B200_N1_ST", st)
+                monkeypatch.setenv("SPARSECORE_B200_N1_RPC", rpc)
+                assert bits_equal(sl.spmm(W, X.to(d)), y), (xs, st, rpc)
+                assert bits_equal(ops._spmm_raw(WT, dY.to(d)), dx), (xs, st, rpc)
+    monkeypatch.delenv("SPARSECORE_B200_N1_RPC")
     monkeypatch.delenv("SPARSECORE_B200_N1_ST")
     monkeypatch.delenv("SPARSECORE_B200_N1_XS")
     monkeypatch.setenv("SPARSECORE_B200_N1", "lane")  # the cp.async lane kernel
