@@ -300,6 +300,12 @@ SL_API int sl_set_regrow_draws(uint64_t* pcg_state, int32_t* has_uint32, uint32_
  * the layer and column-per-token [features, tokens] for the kernels. */
 SL_API int sl_transpose_f32(const float* src, int64_t rows, int64_t cols, float* dst,
                      void* stream);
+/* dst[cols, rows] = src[rows, cols]^T + bias[rows] broadcast along the new
+ * rows: the SparseLinear output transpose with the layer's bias add fused in
+ * (sparselab/nn.py:229-245 adds the bias to the strided Y.t() afterwards).
+ * Each element is one fp32 add, as torch's, so the result is bit-identical. */
+SL_API int sl_transpose_bias_f32(const float* src, int64_t rows, int64_t cols,
+                                 const float* bias, float* dst, void* stream);
 
 /* Fused AdamW over a SparseLinear's live slots (the "fused optimizer over
  * padded values" item of the reference's sparse-training path; the reference

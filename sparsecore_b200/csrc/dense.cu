@@ -16,7 +16,8 @@ constexpr int kRowsPerPass = 8;
 // Scalar path (any shape / alignment).
 __global__ void __launch_bounds__(kTile * kRowsPerPass)
 transpose_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
-                 float* __restrict__ dst, int64_t tiles_c, int64_t n_tiles) {
+                 float* __restrict__ dst, int64_t tiles_c, int64_t n_tiles,
+                 const float* __restrict__ bias) {
     __shared__ float t[kTile][kTile + 1];
     const int tx = threadIdx.x & (kTile - 1), ty = threadIdx.x / kTile;
     for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
@@ -30,7 +31,8 @@ transpose_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
 #pragma unroll
         for (int k = 0; k < kTile; k += kRowsPerPass) {
             const int64_t c = c0 + ty + k, r = r0 + tx;  // dst row c, column r
-            if (c < cols && r < rows) dst[c * rows + r] = t[tx][ty + k];
+            if (c < cols && r < rows)
+                dst[c * rows + r] = bias ? __fadd_rn(t[tx][ty + k], __ldg(bias + r)) : t[tx][ty + k];
         }
         __syncthreads();
     }
@@ -44,7 +46,8 @@ transpose_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
 // segments) even with four tiles in flight per CTA.
 __global__ void __launch_bounds__(256)
 transpose64_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
-                   float* __restrict__ dst, int64_t tiles_c, int64_t n_tiles) {
+                   float* __restrict__ dst, int64_t tiles_c, int64_t n_tiles,
+                   const float* __restrict__ bias) {
     __shared__ float t[64][65];
     const int qx = threadIdx.x & 15, ry = threadIdx.x >> 4;  // float4 column, row (0..15)
     for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
@@ -68,9 +71,16 @@ transpose64_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
         for (int j = 0; j < 4; ++j) {
             const int cc = ry + 16 * j;
             const int64_t c = c0 + cc, r = r0 + 4 * qx;
-            if (c < cols && r < rows)
-                *reinterpret_cast<float4*>(dst + c * rows + r) =
-                    make_float4(t[4 * qx + 0][cc], t[4 * qx + 1][cc], t[4 * qx + 2][cc], t[4 * qx + 3][cc]);
+            if (c < cols && r < rows) {
+                float4 o = make_float4(t[4 * qx + 0][cc], t[4 * qx + 1][cc], t[4 * qx + 2][cc],
+                                       t[4 * qx + 3][cc]);
+                if (bias) {
+                    const float4 b = __ldg(reinterpret_cast<const float4*>(bias + r));
+                    o = make_float4(__fadd_rn(o.x, b.x), __fadd_rn(o.y, b.y), __fadd_rn(o.z, b.z),
+                                    __fadd_rn(o.w, b.w));
+                }
+                *reinterpret_cast<float4*>(dst + c * rows + r) = o;
+            }
         }
         __syncthreads();
     }
@@ -81,27 +91,42 @@ transpose64_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
 
 using namespace slb;
 
-extern "C" int sl_transpose_f32(const float* src, int64_t rows, int64_t cols, float* dst,
-                                void* stream) {
-    if (rows < 0 || cols < 0) return fail(SL_ERR_INVALID, "sl_transpose_f32: negative shape");
+namespace {
+int transpose_impl(const float* src, int64_t rows, int64_t cols, float* dst, const float* bias,
+                   void* stream) {
+    if (rows < 0 || cols < 0) return fail(SL_ERR_INVALID, "sl_transpose: negative shape");
     if (rows == 0 || cols == 0) return SL_OK;
     if (src == nullptr || dst == nullptr)
-        return fail(SL_ERR_INVALID, "sl_transpose_f32: NULL operand");
-    if (src == dst) return fail(SL_ERR_INVALID, "sl_transpose_f32: in-place is not supported");
+        return fail(SL_ERR_INVALID, "sl_transpose: NULL operand");
+    if (src == dst) return fail(SL_ERR_INVALID, "sl_transpose: in-place is not supported");
     const int64_t tiles_c = (cols + kTile - 1) / kTile;
     const int64_t n_tiles = ((rows + kTile - 1) / kTile) * tiles_c;
     int64_t grid = n_tiles;
     const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
     if (grid > cap) grid = cap;
-    if (rows % 4 == 0 && cols % 4 == 0 && aligned16(src) && aligned16(dst)) {
+    if (rows % 4 == 0 && cols % 4 == 0 && aligned16(src) && aligned16(dst) &&
+        (bias == nullptr || aligned16(bias))) {
         const int64_t tc = (cols + 63) / 64, nt = ((rows + 63) / 64) * tc;
         const int64_t g = nt < cap ? nt : cap;
         transpose64_kernel<<<static_cast<unsigned>(g), 256, 0, as_stream(stream)>>>(
-            src, rows, cols, dst, tc, nt);
+            src, rows, cols, dst, tc, nt, bias);
     } else {
         transpose_kernel<<<static_cast<unsigned>(grid), kTile * kRowsPerPass, 0, as_stream(stream)>>>(
-            src, rows, cols, dst, tiles_c, n_tiles);
+            src, rows, cols, dst, tiles_c, n_tiles, bias);
     }
     SL_RETURN_IF_LAUNCH_FAILED("sl_transpose_f32");
     return SL_OK;
+}
+}  // namespace
+
+extern "C" int sl_transpose_f32(const float* src, int64_t rows, int64_t cols, float* dst,
+                                void* stream) {
+    return transpose_impl(src, rows, cols, dst, nullptr, stream);
+}
+
+extern "C" int sl_transpose_bias_f32(const float* src, int64_t rows, int64_t cols,
+                                     const float* bias, float* dst, void* stream) {
+    if (bias == nullptr && rows > 0 && cols > 0)
+        return fail(SL_ERR_INVALID, "sl_transpose_bias_f32: NULL bias");
+    return transpose_impl(src, rows, cols, dst, bias, stream);
 }

@@ -93,9 +93,8 @@ class SparseLinear(nn.Module):
             raise ValueError(f"SparseLinear expects input last dim {self.in_features}, "
                              f"got {orig_shape[-1]}")
         x_flat = x.reshape(-1, self.in_features)
-        y_flat = _SparseLinearFunction.apply(self._values, self._csr, x_flat)
-        if self.bias is not None:
-            y_flat = y_flat + self.bias
+        # The bias add is fused into the output transpose (nn.py:239-241).
+        y_flat = _SparseLinearFunction.apply(self._values, self._csr, x_flat, self.bias)
         return y_flat.reshape(orig_shape[:-1] + (self.out_features,))
 
     @property

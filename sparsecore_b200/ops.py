@@ -138,6 +138,19 @@ def _sddmm_raw(W: PaddedCSR, dY: torch.Tensor, X: torch.Tensor) -> torch.Tensor:
     return dW
 
 
+def _transpose_bias(t: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """[r, c] -> contiguous [c, r] with bias[r] added to every new row
+    (sl_transpose_bias_f32: the layer's bias add fused into the transpose)."""
+    t = t.contiguous()
+    b = bias.detach().to(dtype=torch.float32).contiguous()
+    r, c = t.shape
+    out = torch.empty(c, r, dtype=torch.float32, device=t.device)
+    _launch("transpose", 8 * r * c + 4 * r, 0,
+            lambda: N.call("sl_transpose_bias_f32", N.ptr(t), r, c, N.ptr(b), N.ptr(out),
+                           N.stream_ptr(t.device)))
+    return out
+
+
 def _transpose(t: torch.Tensor) -> torch.Tensor:
     """[r, c] fp32 CUDA tensor -> contiguous [c, r] copy (sl_transpose_f32)."""
     t = t.to(dtype=torch.float32).contiguous()
@@ -200,21 +213,25 @@ class _SparseLinearFunction(torch.autograd.Function):
 
     The reference builds the kernels' column-per-token operand with torch
     copies (``sparselab/nn.py:229-237``: ``x.reshape(-1, in).t().contiguous()``
-    and ``Y.t()`` of the result, leaving a strided output).  Here both
-    directions go through ``sl_transpose_f32`` and the output is returned
-    contiguous, so the surrounding element-wise ops stay vectorised:
+    and ``Y.t()`` of the result, leaving a strided output) and then adds the
+    bias (``nn.py:239-241``).  Here both directions go through the transpose
+    kernel, the bias add is fused into the output transpose
+    (``sl_transpose_bias_f32``), and the output is returned contiguous, so
+    the surrounding element-wise ops stay vectorised:
 
-        forward:  X = x^T;  Y = W.X (sl_spmm_fwd);  y = Y^T
+        forward:  X = x^T;  Y = W.X (sl_spmm_fwd);  y = Y^T (+ bias)
         backward: dY = dy^T;  dW = SDDMM(dY, X);  dX = W^T.dY (cached
-                  transpose);  dx = dX^T
+                  transpose);  dx = dX^T;  dbias = dy.sum(0)
 
-    Transposes are exact copies, so every value equals ``_SpMMFunction``'s on
-    ``x.t()``.  Inputs ``(W_values, W, x)``; backward returns
-    ``(dW_values[total_capacity], None, dx)``.
+    Transposes are exact copies and the bias add is one fp32 add per element,
+    so every value equals ``_SpMMFunction``'s on ``x.t()`` plus torch's bias
+    add, and dbias is the reduction autograd makes for a broadcast add.
+    Inputs ``(W_values, W, x, bias)`` (bias may be None); backward returns
+    ``(dW_values[total_capacity], None, dx, dbias)``.
     """
 
     @staticmethod
-    def forward(ctx, W_values, W, x):
+    def forward(ctx, W_values, W, x, bias=None):
         if x.device.type != "cuda" or x.device != W.device:
             raise RuntimeError(f"SparseLinear: input must be on {W.device} (got {x.device}); "
                                f"sparsecore_b200 has no CPU path.")
@@ -222,7 +239,11 @@ class _SparseLinearFunction(torch.autograd.Function):
         ctx.save_for_backward(W_values, X)
         ctx.W = W
         ctx.param = W_values
-        return _transpose(_spmm_raw(W, X))
+        Y = _spmm_raw(W, X)
+        if bias is not None and bias.dtype == torch.float32 and bias.device == Y.device:
+            return _transpose_bias(Y, bias)
+        y = _transpose(Y)
+        return y if bias is None else y + bias
 
     @staticmethod
     def backward(ctx, dy):
@@ -233,7 +254,8 @@ class _SparseLinearFunction(torch.autograd.Function):
         dx = None
         if ctx.needs_input_grad[2]:
             dx = _transpose(_spmm_raw(_cached_transpose(W), dY, kind="spmm_dx"))
-        return dW, None, dx
+        db = dy.sum(0) if len(ctx.needs_input_grad) > 3 and ctx.needs_input_grad[3] else None
+        return dW, None, dx, db
 
 
 # ── weight gradient off the critical path ───────────────────────────────

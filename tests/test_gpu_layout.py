@@ -177,3 +177,46 @@ def test_dense_transpose_kernel_exact():
     for r, c in [(1, 1), (33, 65), (1000, 7), (7, 1000), (512, 3072), (68, 132), (4, 200), (260, 4)]:
         a = torch.randn(r, c, generator=g).cuda()
         assert torch.equal(ops._transpose(a), a.t().contiguous()), (r, c)
+
+
+def test_transpose_with_bias_matches_torch_add():
+    """sl_transpose_bias_f32 (the SparseLinear output transpose with the bias
+    add fused in) equals torch's transpose followed by ``+ bias`` bit for bit,
+    on the scalar path (odd shapes) and the float4 path."""
+    from sparsecore_b200 import ops
+
+    from gpu_helpers import bits_equal
+
+    g = torch.Generator().manual_seed(6)
+    for r, c in [(1, 1), (33, 65), (1000, 7), (512, 3072), (68, 132), (260, 4)]:
+        a = torch.randn(r, c, generator=g).cuda()
+        b = torch.randn(r, generator=g).cuda()
+        assert bits_equal(ops._transpose_bias(a, b), a.t().contiguous() + b), (r, c)
+
+
+@pytest.mark.parametrize("T,fin,fout", [(37, 96, 48), (256, 384, 1152), (130, 99, 77)])
+def test_sparse_linear_fused_bias_matches_unfused(T, fin, fout):
+    """A SparseLinear with a bias (its output transpose adds the bias) gives
+    the same output and gradients, bit for bit, as the bias-free layer plus
+    torch's broadcast add: y, dx, dW and dbias."""
+    import sparsecore_b200 as sl
+    from sparsecore_b200.ops import _SparseLinearFunction
+
+    from gpu_helpers import bits_equal
+
+    torch.manual_seed(T)
+    layer = sl.SparseLinear(fin, fout, sparsity=0.8, bias=True, device=dev())
+    x = torch.randn(T, fin, device=dev())
+    gy = torch.randn(T, fout, device=dev())
+    x1 = x.clone().requires_grad_(True)
+    y1 = layer(x1)
+    y1.backward(gy)
+    g1 = (y1.detach(), x1.grad, layer._values.grad.clone(), layer.bias.grad.clone())
+    layer.zero_grad(set_to_none=True)
+    x2 = x.clone().requires_grad_(True)
+    y2 = _SparseLinearFunction.apply(layer._values, layer._csr, x2) + layer.bias
+    y2.backward(gy)
+    torch.cuda.synchronize()
+    g2 = (y2.detach(), x2.grad, layer._values.grad, layer.bias.grad)
+    for a, b, name in zip(g1, g2, ("y", "dx", "dW", "dbias")):
+        assert bits_equal(a, b), name
