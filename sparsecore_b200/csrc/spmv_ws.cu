@@ -279,12 +279,11 @@ int launch_spmv_ws(const sl_csr* W, const float* X, int64_t K, float* Y, cudaStr
     const double row_bytes = 8.0 * static_cast<double>(W->total_capacity) / 1.2 / W->nrows;
     bool ks = K <= kMaxKs && 4.0 * K <= 0.5 * 32.0 * row_bytes;
     if (const char* e = std::getenv("SPARSECORE_B200_N1_XS")) ks = (e[0] == '1') && K <= kMaxKs;
-    // Rows per CTA: 16 when 32-row CTAs would not give every SM one and the
-    // rows are long (about 1024 slots or more), so each SM gets two CTAs and
-    // twice the copies in flight.  Measured on 4096 x 4096: 4% faster at 50%
-    // sparsity, 1% slower at 80%, 7% slower at 90% (shorter rows leave the
-    // split CTAs too little to overlap).  SPARSECORE_B200_N1_RPC=16|32.
-    int rpc = (warps <= num_sms() && row_bytes >= 8192.0) ? 16 : 32;
+    // Rows per CTA: 32.  16-row CTAs (two per SM when rows are few) measured
+    // on B200: 4096 x 4096 at 50% sparsity 4% faster, at 90% 7% slower; the
+    // dX of 16384 x 4096 (W^T: 4096 rows of 1600-8200 slots, X staged per
+    // CTA) 1.6x slower.  Kept behind SPARSECORE_B200_N1_RPC=16 (tests).
+    int rpc = 32;
     if (const char* e = std::getenv("SPARSECORE_B200_N1_RPC")) rpc = std::atoi(e) == 16 ? 16 : 32;
     if (rpc == 16) return st == 8 ? launch_ws_x<8, 16>(W, X, K, Y, s, ks) : launch_ws_x<4, 16>(W, X, K, Y, s, ks);
     return st == 8 ? launch_ws_x<8, 32>(W, X, K, Y, s, ks) : launch_ws_x<4, 32>(W, X, K, Y, s, ks);
