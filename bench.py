@@ -721,9 +721,11 @@ def main():
             probe = torch.ones(1, device=torch.device("cuda", local_rank))
             dist.all_reduce(probe)
             ver = ".".join(str(v) for v in torch.cuda.nccl.version())
-            print(f"NCCL communicator: rank {rank} of {world} on cuda:{local_rank} "
-                  f"({torch.cuda.get_device_name(local_rank)}), NCCL {ver}, all-reduce check "
-                  f"{int(probe.item())} == {world}", file=sys.stderr, flush=True)
+            # One write per line, so lines of concurrent ranks do not interleave.
+            msg = (f"NCCL communicator: rank {rank} of {world} on cuda:{local_rank} "
+                   f"({torch.cuda.get_device_name(local_rank)}), NCCL {ver}, all-reduce check "
+                   f"{int(probe.item())} == {world}\n")
+            os.write(sys.stderr.fileno(), msg.encode())
         line = run_ours(args, rank, world, local_rank)
         if world > 1:
             dist.barrier()
