@@ -100,6 +100,17 @@ SL_API int sl_spmm_fwd(const sl_csr* W, const float* X, int64_t K, int64_t N,
  * runs, else by a second pass.  Y is kept for the GELU backward. */
 SL_API int sl_spmm_fwd_gelu(const sl_csr* W, const float* X, int64_t K, int64_t N,
                      float* Y, float* H, void* stream);
+/* Forward with a SparseLinear's bias and activation fused into the kernel
+ * (sparselab/nn.py:239-241 adds the bias after the layer; the activation of
+ * an FFN pair runs as a separate torch op):
+ *   Y[M,N] = W . X + bias[M] (broadcast along N; bias may be NULL), and
+ *   H[M,N] = act(Y) for act = 1 (ReLU: negative -> 0, NaN kept) or 2 (GELU,
+ *   exact erf, torch's rounding); act = 0 writes no H (H may be NULL).
+ * The bias add is one fp32 add per element, as torch's, so Y and H are
+ * bit-identical to the unfused ops.  Fused into the X-stationary and
+ * row-gather kernels' epilogue, else applied by a second pass. */
+SL_API int sl_spmm_fwd_act(const sl_csr* W, const float* X, int64_t K, int64_t N,
+                    const float* bias, int act, float* Y, float* H, void* stream);
 
 /* ── SDDMM weight gradient ────────────────────────────────────────────────
  * dW[slot] = <dY[i,:], X[col[slot],:]> for live slots of row i, 0 for

@@ -51,6 +51,7 @@ SIGNATURES: dict[str, tuple] = {
     "sl_selftest_bounded_wait": (I32, [I64, P]),
     "sl_spmm_fwd": (I32, [P, P, I64, I64, P, P]),
     "sl_spmm_fwd_gelu": (I32, [P, P, I64, I64, P, P, P]),
+    "sl_spmm_fwd_act": (I32, [P, P, I64, I64, P, I32, P, P, P]),
     "sl_sddmm_dw": (I32, [P, P, P, I64, P, P]),
     "sl_transpose_scratch_bytes": (I64, [I64, I64]),
     "sl_transpose_count": (I32, [P, F64, P, P, P, P, P, P]),
@@ -145,7 +146,7 @@ def ptr(t: torch.Tensor | None) -> P:
 
 # Kernels each entry point launches (for launch accounting).
 KERNELS_PER_CALL = {
-    "sl_spmm_fwd": 1, "sl_spmm_fwd_gelu": 1, "sl_transpose_bias_f32": 1, "sl_sddmm_dw": 1, "sl_transpose_count": 3, "sl_transpose_fill": 2,
+    "sl_spmm_fwd": 1, "sl_spmm_fwd_gelu": 1, "sl_spmm_fwd_act": 1, "sl_transpose_bias_f32": 1, "sl_sddmm_dw": 1, "sl_transpose_count": 3, "sl_transpose_fill": 2,
     "sl_transpose_with_perm_noalloc": 5,
     "sl_values_gather": 1, "sl_dense_count": 2, "sl_dense_fill": 1, "sl_capacity_scan": 1,
     "sl_to_dense": 1, "sl_check_invariants": 2, "sl_dense_grad": 1, "sl_rigl_prep": 1, "sl_rigl_candidates": 1, "sl_rigl_merge": 1, "sl_dst_threshold": 9,

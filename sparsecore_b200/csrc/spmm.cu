@@ -62,6 +62,37 @@ __device__ __forceinline__ float gelu_erf(float x) {
     return __fmul_rn(__fmul_rn(x, 0.5f), __fadd_rn(1.0f, erff(__fmul_rn(x, kAlpha))));
 }
 
+// Forward epilogue: Y = acc (+ bias[row]) and, with H, H = act(Y); act 0 =
+// none, 1 = ReLU (torch.relu: negative -> 0, NaN stays), 2 = GELU (exact erf).
+// The bias add is one fp32 add, as torch's broadcast add after the layer.
+struct Epi {
+    float* H = nullptr;
+    const float* bias = nullptr;
+    int act = 0;
+};
+__device__ __forceinline__ float epi_act(float v, int act) {
+    if (act == 2) return gelu_erf(v);
+    if (act == 1) return v < 0.0f ? 0.0f : v;
+    return v;
+}
+__device__ __forceinline__ void epi_store4(const Epi& epi, float* y, int64_t off, int row, float a0,
+                                           float a1, float a2, float a3) {
+    if (epi.bias) {
+        const float b = __ldg(epi.bias + row);
+        a0 = __fadd_rn(a0, b); a1 = __fadd_rn(a1, b); a2 = __fadd_rn(a2, b); a3 = __fadd_rn(a3, b);
+    }
+    *reinterpret_cast<float4*>(y + off) = make_float4(a0, a1, a2, a3);
+    if (epi.H)
+        *reinterpret_cast<float4*>(epi.H + off) =
+            make_float4(epi_act(a0, epi.act), epi_act(a1, epi.act), epi_act(a2, epi.act),
+                        epi_act(a3, epi.act));
+}
+__device__ __forceinline__ void epi_store1(const Epi& epi, float* y, int64_t off, int row, float a) {
+    if (epi.bias) a = __fadd_rn(a, __ldg(epi.bias + row));
+    y[off] = a;
+    if (epi.H) epi.H[off] = epi_act(a, epi.act);
+}
+
 // Slot staging.  Per chunk the warp moves slots [base, base+CH) of each of
 // its RPW rows into shared memory (row r at st + r*(CH+1)).  The loads of a
 // chunk go to registers first (ITER = RPW*CH/32 per lane, one row-run of CH
@@ -119,7 +150,7 @@ __global__ void __launch_bounds__(kFwdThreads)
 spmm_fwd_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
                 const int32_t* __restrict__ row_nnz, const int32_t* __restrict__ cols,
                 const float* __restrict__ vals, const float* __restrict__ X,
-                float* __restrict__ Y, int64_t n_tiles, int64_t n_items, float* __restrict__ H) {
+                float* __restrict__ Y, int64_t n_tiles, int64_t n_items, Epi epi) {
     constexpr int RPW = 32 / LPR;
     constexpr int TILE = LPR * VEC * CPL;
     constexpr int CH = ChunkOf<LPR>::value;
@@ -181,22 +212,15 @@ spmm_fwd_kernel(int M, int64_t N, const int32_t* __restrict__ row_start,
         }
 
         if (valid) {
-            float* yr = Y + static_cast<int64_t>(row) * N;
 #pragma unroll
             for (int cc = 0; cc < CPL; ++cc) {
                 const int64_t j = jbase + static_cast<int64_t>(cc) * LPR * VEC;
                 if (j < N) {
-                    if constexpr (VEC == 4) {
-                        *reinterpret_cast<float4*>(yr + j) =
-                            make_float4(acc[cc][0], acc[cc][1], acc[cc][2], acc[cc][3]);
-                        if (H)
-                            *reinterpret_cast<float4*>(H + static_cast<int64_t>(row) * N + j) =
-                                make_float4(gelu_erf(acc[cc][0]), gelu_erf(acc[cc][1]),
-                                            gelu_erf(acc[cc][2]), gelu_erf(acc[cc][3]));
-                    } else {
-                        yr[j] = acc[cc][0];
-                        if (H) H[static_cast<int64_t>(row) * N + j] = gelu_erf(acc[cc][0]);
-                    }
+                    if constexpr (VEC == 4)
+                        epi_store4(epi, Y, static_cast<int64_t>(row) * N + j, row, acc[cc][0],
+                                   acc[cc][1], acc[cc][2], acc[cc][3]);
+                    else
+                        epi_store1(epi, Y, static_cast<int64_t>(row) * N + j, row, acc[cc][0]);
                 }
             }
         }
@@ -721,7 +745,7 @@ int dispatch_rowwarp(const sl_csr* W, const float* X, int64_t N, float* Y, cudaS
 
 template <int VEC, int LPR, int CPL>
 int launch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_t s,
-               float* H = nullptr) {
+               Epi epi = Epi{}) {
     constexpr int RPW = 32 / LPR;
     constexpr int TILE = LPR * VEC * CPL;
     const int M = static_cast<int>(W->nrows);
@@ -736,7 +760,7 @@ int launch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_
     if (blocks > max_blocks) blocks = max_blocks;
     note_kernel("spmm_fwd_kernel");
     spmm_fwd_kernel<VEC, LPR, CPL><<<static_cast<unsigned>(blocks), threads, 0, s>>>(
-        M, N, W->row_start, W->row_nnz, W->col_indices, W->values, X, Y, n_tiles, n_items, H);
+        M, N, W->row_start, W->row_nnz, W->col_indices, W->values, X, Y, n_tiles, n_items, epi);
     SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd");
     return SL_OK;
 }
@@ -744,7 +768,7 @@ int launch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_
 // Lane layout by the number of column vectors per row.
 template <int VEC>
 int dispatch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStream_t s,
-                 float* H = nullptr) {
+                 Epi epi = Epi{}) {
     const int64_t nv = (N + VEC - 1) / VEC;
     // SPARSECORE_B200_FWD_TILE=32|64|128|256: column tile of the row-gather
     // kernel at large N (measurements; narrower tiles make the resident
@@ -752,18 +776,18 @@ int dispatch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStrea
     if (const char* e = std::getenv("SPARSECORE_B200_FWD_TILE")) {
         const int t = std::atoi(e);
         if (VEC == 4 && nv >= 64) {
-            if (t == 32) return launch_fwd<VEC, 8, 1>(W, X, N, Y, s, H);
-            if (t == 64) return launch_fwd<VEC, 16, 1>(W, X, N, Y, s, H);
-            if (t == 128) return launch_fwd<VEC, 32, 1>(W, X, N, Y, s, H);
+            if (t == 32) return launch_fwd<VEC, 8, 1>(W, X, N, Y, s, epi);
+            if (t == 64) return launch_fwd<VEC, 16, 1>(W, X, N, Y, s, epi);
+            if (t == 128) return launch_fwd<VEC, 32, 1>(W, X, N, Y, s, epi);
         }
     }
-    if (nv >= 64) return launch_fwd<VEC, 32, 2>(W, X, N, Y, s, H);
-    if (nv > 16) return launch_fwd<VEC, 32, 1>(W, X, N, Y, s, H);
-    if (nv > 8) return launch_fwd<VEC, 16, 1>(W, X, N, Y, s, H);
-    if (nv > 4) return launch_fwd<VEC, 8, 1>(W, X, N, Y, s, H);
-    if (nv > 2) return launch_fwd<VEC, 4, 1>(W, X, N, Y, s, H);
-    if (nv > 1) return launch_fwd<VEC, 2, 1>(W, X, N, Y, s, H);
-    return launch_fwd<VEC, 1, 1>(W, X, N, Y, s, H);
+    if (nv >= 64) return launch_fwd<VEC, 32, 2>(W, X, N, Y, s, epi);
+    if (nv > 16) return launch_fwd<VEC, 32, 1>(W, X, N, Y, s, epi);
+    if (nv > 8) return launch_fwd<VEC, 16, 1>(W, X, N, Y, s, epi);
+    if (nv > 4) return launch_fwd<VEC, 8, 1>(W, X, N, Y, s, epi);
+    if (nv > 2) return launch_fwd<VEC, 4, 1>(W, X, N, Y, s, epi);
+    if (nv > 1) return launch_fwd<VEC, 2, 1>(W, X, N, Y, s, epi);
+    return launch_fwd<VEC, 1, 1>(W, X, N, Y, s, epi);
 }
 
 
@@ -793,7 +817,7 @@ __global__ void __launch_bounds__(xs_threads<LPR>())
 spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
                const int32_t* __restrict__ row_start, const int32_t* __restrict__ row_nnz,
                const int32_t* __restrict__ cols, const float* __restrict__ vals,
-               float* __restrict__ Y, float* __restrict__ H, int nbox, int row_chunks, int64_t n_items,
+               float* __restrict__ Y, Epi epi, int nbox, int row_chunks, int64_t n_items,
                int64_t items_per_cta, unsigned* status) {
     constexpr int TN = 4 * LPR;
     constexpr int RPW = 32 / LPR;
@@ -881,14 +905,9 @@ spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
                 }
                 __syncwarp();
             }
-            if (valid && j < N) {
-                *reinterpret_cast<float4*>(Y + static_cast<int64_t>(row) * N + j) =
-                    make_float4(acc[0], acc[1], acc[2], acc[3]);
-                if (H)
-                    *reinterpret_cast<float4*>(H + static_cast<int64_t>(row) * N + j) =
-                        make_float4(gelu_erf(acc[0]), gelu_erf(acc[1]), gelu_erf(acc[2]),
-                                    gelu_erf(acc[3]));
-            }
+            if (valid && j < N)
+                epi_store4(epi, Y, static_cast<int64_t>(row) * N + j, row, acc[0], acc[1], acc[2],
+                           acc[3]);
         }
     }
 }
@@ -915,7 +934,7 @@ int xs_lanes_for(int64_t K) {
 
 template <int LPR>
 int launch_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, cudaStream_t s,
-              float* H = nullptr) {
+              Epi epi = Epi{}) {
     constexpr int TN = 4 * LPR;
     constexpr int RPW = 32 / LPR;
     constexpr int kXsWarps = xs_threads<LPR>() / 32;
@@ -943,7 +962,7 @@ int launch_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, c
     grid = (n_items + per_cta - 1) / per_cta;
     note_kernel("spmm_xs_kernel");
     spmm_xs_kernel<LPR><<<static_cast<unsigned>(grid), xs_threads<LPR>(), smem, s>>>(
-        map, M, N, W->row_start, W->row_nnz, W->col_indices, W->values, Y, H, nbox, row_chunks,
+        map, M, N, W->row_start, W->row_nnz, W->col_indices, W->values, Y, epi, nbox, row_chunks,
         n_items, per_cta, status);
     SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd (x-stationary)");
     return SL_OK;
@@ -961,7 +980,7 @@ int fwd_path() {
 
 // Returns -1 when the X-stationary path does not apply.
 int try_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, cudaStream_t s,
-           bool forced, float* H = nullptr) {
+           bool forced, Epi epi = Epi{}) {
     if (N < 256 || N % 4 != 0 || !aligned16(X) || !aligned16(Y) || K < 1 || K > INT_MAX) return -1;
     // Measured on B200 (config-4/5 shapes, N = 16384): with 64- or 128-column
     // tiles (K <= 768) the X-stationary kernel beats the row-gather kernel on
@@ -981,9 +1000,9 @@ int try_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, cuda
         if (v == 64 && xs_lanes_for64(K)) tn = 64;
         if (v == 128 && xs_lanes_for128(K)) tn = 128;
     }
-    if (tn == 128) return launch_xs<32>(W, X, K, N, Y, s, H);
-    if (tn == 64) return launch_xs<16>(W, X, K, N, Y, s, H);
-    if (tn == 32) return launch_xs<8>(W, X, K, N, Y, s, H);
+    if (tn == 128) return launch_xs<32>(W, X, K, N, Y, s, epi);
+    if (tn == 64) return launch_xs<16>(W, X, K, N, Y, s, epi);
+    if (tn == 32) return launch_xs<8>(W, X, K, N, Y, s, epi);
     return -1;
 }
 }  // namespace
@@ -993,24 +1012,32 @@ using namespace slb;
 
 namespace slb {
 namespace {
-__global__ void __launch_bounds__(256) gelu_kernel(const float* __restrict__ Y, float* __restrict__ H,
-                                                   int64_t n) {
+// Epilogue as a second pass, for the decompositions without one: Y += bias
+// (in place) and H = act(Y).
+__global__ void __launch_bounds__(256) epi_kernel(float* __restrict__ Y, Epi epi, int64_t N,
+                                                  int64_t n) {
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-        H[i] = gelu_erf(Y[i]);
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float v = Y[i];
+        if (epi.bias) {
+            v = __fadd_rn(v, __ldg(epi.bias + i / N));
+            Y[i] = v;
+        }
+        if (epi.H) epi.H[i] = epi_act(v, epi.act);
+    }
 }
 
-// The forward dispatch; with H != nullptr also H = gelu(Y), fused into the
-// epilogue of the X-stationary and row-gather kernels, else a second pass.
-int spmm_fwd_impl(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, float* H,
+// The forward dispatch with its epilogue (bias, activation) fused into the
+// X-stationary and row-gather kernels, else applied by a second pass.
+int spmm_fwd_impl(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, Epi epi,
                   cudaStream_t s) {
     const int path = fwd_path();
     int rc = -1;
-    if (path != kPathRows) rc = try_xs(W, X, K, N, Y, s, path == kPathXs, H);
+    if (path != kPathRows) rc = try_xs(W, X, K, N, Y, s, path == kPathXs, epi);
     if (rc >= 0) return rc;
     if (N >= 128) {
-        const bool vec4 = (N % 4 == 0) && aligned16(X) && aligned16(Y) && (H == nullptr || aligned16(H));
-        return vec4 ? dispatch_fwd<4>(W, X, N, Y, s, H) : dispatch_fwd<1>(W, X, N, Y, s, H);
+        const bool vec4 = (N % 4 == 0) && aligned16(X) && aligned16(Y) && (epi.H == nullptr || aligned16(epi.H));
+        return vec4 ? dispatch_fwd<4>(W, X, N, Y, s, epi) : dispatch_fwd<1>(W, X, N, Y, s, epi);
     }
     if (N == 1 && spmv_lane_enabled(W)) {
         // Measured on B200 (4096 and 16384 rows x 4096, 50-99%): the
@@ -1033,12 +1060,12 @@ int spmm_fwd_impl(const sl_csr* W, const float* X, int64_t K, int64_t N, float* 
     // selects the staged kernel (tests).
     if (rc < 0 && N == 32 && gather32_forced()) rc = launch_gather32_fwd(W, X, Y, s);
     if (rc < 0) rc = dispatch_rowwarp(W, X, N, Y, s);
-    if (rc == SL_OK && H != nullptr) {
+    if (rc == SL_OK && (epi.H != nullptr || epi.bias != nullptr)) {
         const int64_t n = W->nrows * N;
         int64_t blocks = (n + 255) / 256;
         const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
-        gelu_kernel<<<static_cast<unsigned>(blocks < cap ? blocks : cap), 256, 0, s>>>(Y, H, n);
-        SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd_gelu");
+        epi_kernel<<<static_cast<unsigned>(blocks < cap ? blocks : cap), 256, 0, s>>>(Y, epi, N, n);
+        SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd_act");
     }
     return rc;
 }
@@ -1068,7 +1095,7 @@ extern "C" int sl_spmm_fwd(const sl_csr* W, const float* X, int64_t K, int64_t N
     cudaStream_t s = as_stream(stream);
     if (K == 0) return cuda_status(cudaMemsetAsync(Y, 0, sizeof(float) * W->nrows * N, s),
                                    "sl_spmm_fwd memset");
-    return spmm_fwd_impl(W, X, K, N, Y, nullptr, s);
+    return spmm_fwd_impl(W, X, K, N, Y, Epi{}, s);
 }
 
 extern "C" int sl_spmm_fwd_gelu(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y,
@@ -1083,5 +1110,34 @@ extern "C" int sl_spmm_fwd_gelu(const sl_csr* W, const float* X, int64_t K, int6
             return e;
         return cuda_status(cudaMemsetAsync(H, 0, sizeof(float) * W->nrows * N, s), "sl_spmm_fwd_gelu memset");
     }
-    return spmm_fwd_impl(W, X, K, N, Y, H, s);
+    Epi epi;
+    epi.H = H;
+    epi.act = 2;
+    return spmm_fwd_impl(W, X, K, N, Y, epi, s);
+}
+
+extern "C" int sl_spmm_fwd_act(const sl_csr* W, const float* X, int64_t K, int64_t N,
+                               const float* bias, int act, float* Y, float* H, void* stream) {
+    const int rc = check_fwd_args(W, X, K, N, Y, "sl_spmm_fwd_act");
+    if (rc < 0) return SL_OK;
+    if (rc != SL_OK) return rc;
+    if (act < 0 || act > 2) return fail(SL_ERR_INVALID, "sl_spmm_fwd_act: act must be 0 (none), 1 (relu) or 2 (gelu)");
+    if (act != 0 && H == nullptr) return fail(SL_ERR_INVALID, "sl_spmm_fwd_act: NULL H with an activation");
+    cudaStream_t s = as_stream(stream);
+    Epi epi;
+    epi.H = act != 0 ? H : nullptr;
+    epi.bias = bias;
+    epi.act = act;
+    if (K == 0) {  // Y = bias (or 0), H = act(Y): the second pass over a zeroed Y
+        if (int e = cuda_status(cudaMemsetAsync(Y, 0, sizeof(float) * W->nrows * N, s), "sl_spmm_fwd_act memset"))
+            return e;
+        if (epi.H == nullptr && epi.bias == nullptr) return SL_OK;
+        const int64_t n = W->nrows * N;
+        int64_t blocks = (n + 255) / 256;
+        const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
+        epi_kernel<<<static_cast<unsigned>(blocks < cap ? blocks : cap), 256, 0, s>>>(Y, epi, N, n);
+        SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd_act");
+        return SL_OK;
+    }
+    return spmm_fwd_impl(W, X, K, N, Y, epi, s);
 }

@@ -111,17 +111,21 @@ class SparseLinear(nn.Module):
 
 
 def _plain(layer: SparseLinear) -> bool:
-    return (layer.bias is None and not layer._forward_hooks and not layer._forward_pre_hooks
-            and not layer._backward_hooks and not getattr(layer, "_backward_pre_hooks", None))
+    return (not layer._forward_hooks and not layer._forward_pre_hooks
+            and not layer._backward_hooks and not getattr(layer, "_backward_pre_hooks", None)
+            and (layer.bias is None or (layer.bias.dtype == torch.float32
+                                        and layer.bias.device == layer._csr.device)))
 
 
 def sparse_mlp(x: torch.Tensor, fc1: SparseLinear, fc2: SparseLinear,
                activation: str = "gelu") -> torch.Tensor:
     """``fc2(act(fc1(x)))`` for two SparseLinears with ``activation`` in
-    {"gelu", "relu"}.  When both layers are bias-free and carry no module
-    hooks (RigL's gradient capture uses hooks), the hidden activation stays
-    in the kernels' column-per-token layout (``ops._SparseMLPFunction``);
-    otherwise the two layers are called as modules.  Same values either way.
+    {"gelu", "relu"}.  When neither layer carries module hooks (RigL's
+    gradient capture uses hooks), the hidden activation stays in the
+    kernels' column-per-token layout (``ops._SparseMLPFunction``), with
+    fc1's bias and the activation fused into its forward kernel and fc2's
+    bias into the output transpose; otherwise the two layers are called as
+    modules.  Same values either way.
     """
     if activation not in ("gelu", "relu"):
         raise ValueError(f"sparse_mlp: activation must be 'gelu' or 'relu', got {activation!r}")
@@ -134,5 +138,5 @@ def sparse_mlp(x: torch.Tensor, fc1: SparseLinear, fc2: SparseLinear,
         return fc2(h)
     shp = x.shape
     y = _SparseMLPFunction.apply(fc1._values, fc2._values, x.reshape(-1, fc1.in_features),
-                                 fc1._csr, fc2._csr, activation)
+                                 fc1._csr, fc2._csr, activation, fc1.bias, fc2.bias)
     return y.reshape(shp[:-1] + (fc2.out_features,))

@@ -126,6 +126,26 @@ def _spmm_gelu_raw(W: PaddedCSR, X: torch.Tensor) -> tuple[torch.Tensor, torch.T
     return Y, H
 
 
+_ACT_CODE = {"relu": 1, "gelu": 2}
+
+
+def _spmm_act_raw(W: PaddedCSR, X: torch.Tensor, bias: torch.Tensor | None,
+                  act: str) -> tuple[torch.Tensor, torch.Tensor]:
+    """(Y, act(Y)) with Y = W.X + bias[:, None] (bias may be None); the bias
+    and the activation fused into the forward kernel's epilogue where the
+    decomposition allows (``sl_spmm_fwd_act``)."""
+    M = W.nrows
+    K, Ncol = X.shape
+    Y = torch.empty(M, Ncol, dtype=torch.float32, device=X.device)
+    H = torch.empty_like(Y)
+    b = None if bias is None else bias.detach().to(dtype=torch.float32).contiguous()
+    nnz = W.nnz
+    _launch("spmm_fwd", 8 * nnz + 8 * M + 4 * K * Ncol + 8 * M * Ncol, 2 * nnz * Ncol,
+            lambda: N.call("sl_spmm_fwd_act", W._abi_ref(), N.ptr(X), K, Ncol, N.ptr(b),
+                           _ACT_CODE[act], N.ptr(Y), N.ptr(H), W._stream()))
+    return Y, H
+
+
 def _sddmm_raw(W: PaddedCSR, dY: torch.Tensor, X: torch.Tensor) -> torch.Tensor:
     """dW[total_capacity] at live slots (padding 0)."""
     dW = torch.empty(W.total_capacity, dtype=torch.float32, device=dY.device)
@@ -362,26 +382,25 @@ def _weight_grad(W: PaddedCSR, dY: torch.Tensor, X: torch.Tensor, param, needed:
 
 
 class _SparseMLPFunction(torch.autograd.Function):
-    """Two bias-free SparseLinears with an element-wise activation between
-    them, ``y = W2 . act(W1 . x^T)``, keeping the hidden activation in the
-    kernels' column-per-token layout: the transposes of the hidden tensor
-    that two separate SparseLinear calls would make (one each way, forward
-    and backward) are skipped.  Every value equals the unfused composition
-    (the activation and its backward are element-wise)."""
+    """Two SparseLinears with an element-wise activation between them,
+    ``y = (W2 . act(W1 . x^T + b1) + b2)^T`` (either bias may be None),
+    keeping the hidden activation in the kernels' column-per-token layout:
+    the transposes of the hidden tensor that two separate SparseLinear calls
+    would make (one each way, forward and backward) are skipped.  b1 and the
+    activation run in the first forward kernel's epilogue, b2 in the output
+    transpose.  Every value equals the unfused composition: the bias adds and
+    the activation and its backward are element-wise, and each bias gradient
+    is the token-major reduction autograd makes for the broadcast add."""
 
     @staticmethod
-    def forward(ctx, v1, v2, x, W1, W2, act):
+    def forward(ctx, v1, v2, x, W1, W2, act, b1=None, b2=None):
         X = _transpose(x)
-        if act == "gelu":
-            Y1, H = _spmm_gelu_raw(W1, X)  # GELU in the forward kernel's epilogue
-        else:
-            Y1 = _spmm_raw(W1, X)
-            H = torch.relu(Y1)
-        Y2 = _spmm_raw(W2, H)
+        Y1, H = _spmm_act_raw(W1, X, b1, act)
         ctx.save_for_backward(X, Y1, H)
         ctx.W1, ctx.W2, ctx.act = W1, W2, act
         ctx.p1, ctx.p2 = v1, v2
-        return _transpose(Y2)
+        Y2 = _spmm_raw(W2, H)
+        return _transpose(Y2) if b2 is None else _transpose_bias(Y2, b2)
 
     @staticmethod
     def backward(ctx, dy):
@@ -398,7 +417,10 @@ class _SparseMLPFunction(torch.autograd.Function):
         dx = None
         if ctx.needs_input_grad[2]:
             dx = _transpose(_spmm_raw(_cached_transpose(W1), dY1, kind="spmm_dx"))
-        return dW1, dW2, dx, None, None, None
+        ng = ctx.needs_input_grad
+        db1 = _transpose(dY1).sum(0) if len(ng) > 6 and ng[6] else None
+        db2 = dy.sum(0) if len(ng) > 7 and ng[7] else None
+        return dW1, dW2, dx, None, None, None, db1, db2
 
 
 def spmm(W: PaddedCSR, X: torch.Tensor, *, kernel: str = "auto") -> torch.Tensor:
