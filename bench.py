@@ -40,7 +40,7 @@ def parse():
                     help="sequences per CPU sample step (default: the configuration's full batch)")
     ap.add_argument("--kernel", default=None,
                     help="profiling mode: SHAPE:KIND:N runs 2 launches of one kernel "
-                         "(SHAPE in %s or MxK@sparsity; KIND fwd|dw|dx|transpose|densegrad, or "
+                         "(SHAPE in %s or MxK@sparsity; KIND fwd|dw|dx|transpose|dtranspose|densegrad, or "
                          "set|rigl for two router updates)" % list(SHAPES))
     ap.add_argument("--workload", choices=["cfg5", "cfg4", "cfg2"], default="cfg5",
                     help="training workload (default cfg5, the headline configuration)")
@@ -122,6 +122,8 @@ def run_kernel_case(spec):
             ops._spmm_raw(WT, dY)
         elif kind == "densegrad":
             sl.dense_grad(dY, X)
+        elif kind == "dtranspose":  # the SparseLinear layout change of an [M, N] activation
+            ops._transpose(dY)
         else:
             sl.transpose_with_perm(W)
     torch.cuda.synchronize()
