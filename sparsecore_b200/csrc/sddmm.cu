@@ -297,7 +297,10 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
                    const int32_t* __restrict__ row_capacity, const int32_t* __restrict__ cols,
                    float* __restrict__ dW, unsigned* status) {
     extern __shared__ unsigned char smem_raw[];
-    float* sbase = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned for the 128-byte swizzle.  The offset is added to the
+    // shared array itself (not through an integer round trip), so the
+    // compiler keeps every access below a shared-memory access.
+    float* sbase = reinterpret_cast<float*>(smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u));
     __shared__ __align__(8) uint64_t full[kTStages];
     __shared__ __align__(8) uint64_t empty[kTStages];
     __shared__ int run_lo[kTMaxRows];
