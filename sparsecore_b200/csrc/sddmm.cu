@@ -454,8 +454,8 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
             float4 acc[kTS];
 #pragma unroll
             for (int t = 0; t < kTS; ++t) acc[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+            int b = (bt * nchunks) % kTStages;  // stage of the batch's first chunk
             for (int kc = 0; kc < nchunks; ++kc) {
-                const int b = (bt * nchunks + kc) % kTStages;
                 if (ok && !mbar_wait(&full[b], (fph >> b) & 1u, status)) ok = false;  // bounded
                 fph ^= 1u << b;
                 const float* sb = sbase + b * stage;
@@ -470,6 +470,7 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[b]);  // this warp is done with stage b
+                b = b + 1 == kTStages ? 0 : b + 1;
             }
 #pragma unroll
             for (int t = 0; t < kTS; ++t) {
@@ -537,16 +538,18 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
         // chunk's first 16 columns (the second 16 are the same ^ 16), packed
         // as (dY << 16) | X; `fresh` bit s = slot s starts a new W row.
         const int qbase = 16 * (quad >> 1) + (quad & 1);
-        int off[kTS];
+        // The float offsets of both 16-column halves, precomputed (no
+        // decode in the chunk loop).
+        int xa[kTS], xb[kTS], ya[kTS];
         unsigned fresh = 0u;
         int prev_r = -1;
 #pragma unroll
         for (int s = 0; s < kTS; ++s) {
             const int rc = ord_rc[qbase + 2 * s];
             const int r = rc >> 16, c = rc & 0xffff;
-            const int yo = r * kTJ + ((q ^ (r & 7)) << 2);
-            const int xo = TR * kTJ + c * kTJ + ((q ^ (c & 7)) << 2);
-            off[s] = (yo << 16) | xo;
+            ya[s] = r * kTJ + ((q ^ (r & 7)) << 2);
+            xa[s] = TR * kTJ + c * kTJ + ((q ^ (c & 7)) << 2);
+            xb[s] = xa[s] ^ 16;
             if (s == 0 || r != prev_r) fresh |= 1u << s;
             prev_r = r;
         }
@@ -554,24 +557,24 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
 #pragma unroll
         for (int s = 0; s < kTS; ++s) acc[s] = make_float4(0.f, 0.f, 0.f, 0.f);
 
+        int b = (bt * nchunks) % kTStages;  // stage of the batch's first chunk
         for (int k = 0; k < nchunks; ++k) {
-            const int b = (bt * nchunks + k) % kTStages;
             if (ok && !mbar_wait(&full[b], (fph >> b) & 1u, status)) ok = false;  // bounded
             fph ^= 1u << b;
             const float* sb = sbase + b * stage;
             float4 d0 = make_float4(0.f, 0.f, 0.f, 0.f), d1 = d0;
 #pragma unroll
             for (int s = 0; s < kTS; ++s) {
-                const int yo = off[s] >> 16, xo = off[s] & 0xffff;
                 if (fresh & (1u << s)) {
-                    d0 = *reinterpret_cast<const float4*>(sb + yo);
-                    d1 = *reinterpret_cast<const float4*>(sb + (yo ^ 16));
+                    d0 = *reinterpret_cast<const float4*>(sb + ya[s]);
+                    d1 = *reinterpret_cast<const float4*>(sb + (ya[s] ^ 16));
                 }
-                fma4(d0, *reinterpret_cast<const float4*>(sb + xo), acc[s]);
-                fma4(d1, *reinterpret_cast<const float4*>(sb + (xo ^ 16)), acc[s]);
+                fma4(d0, *reinterpret_cast<const float4*>(sb + xa[s]), acc[s]);
+                fma4(d1, *reinterpret_cast<const float4*>(sb + xb[s]), acc[s]);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[b]);  // this warp is done with stage b
+            b = b + 1 == kTStages ? 0 : b + 1;
         }
         // acc = acc_a + acc_b, then the horizontal reduction (N % 16 == 0).
 #pragma unroll
