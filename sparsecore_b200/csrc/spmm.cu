@@ -812,7 +812,7 @@ template <int LPR>
 __host__ __device__ constexpr int xs_ch() { return LPR == 32 ? 32 : 16; }
 constexpr int kXsRowsPerItemMul = 4;
 
-template <int LPR>
+template <int LPR, bool PACK>
 __global__ void __launch_bounds__(xs_threads<LPR>())
 spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
                const int32_t* __restrict__ row_start, const int32_t* __restrict__ row_nnz,
@@ -885,23 +885,56 @@ spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
             SlotStager<LPR, kXsCh, XST> sg;
             if (maxnn > 0) sg.load(rs, nn, 0, cols, vals);
             for (int base = 0; base < maxnn; base += kXsCh) {
-                sg.store(st);
+                if constexpr (PACK) {
+                    // Packed staging: per row kXsCh values, then kXsCh 16-bit
+                    // columns (K < 65536), so 8 slots cost three 128-bit
+                    // reads instead of four.
+#pragma unroll
+                    for (int it = 0; it < SlotStager<LPR, kXsCh, XST>::ITER; ++it) {
+                        const int idx = it * 32 + lane;
+                        float* rv = reinterpret_cast<float*>(st + (idx / kXsCh) * XST);
+                        rv[idx % kXsCh] = sg.v[it];
+                        reinterpret_cast<unsigned short*>(rv + kXsCh)[idx % kXsCh] =
+                            static_cast<unsigned short>(sg.c[it]);
+                    }
+                } else {
+                    sg.store(st);
+                }
                 __syncwarp();
                 if (base + kXsCh < maxnn) sg.load(rs, nn, base + kXsCh, cols, vals);
                 const int cnt = min(kXsCh, nn - base);
                 int t = 0;
+                if constexpr (PACK) {
+                    const float* vrow = reinterpret_cast<const float*>(my);
+                    const unsigned short* crow = reinterpret_cast<const unsigned short*>(vrow + kXsCh);
+                    for (; t + 8 <= cnt; t += 8) {
+                        const uint4 cw = *reinterpret_cast<const uint4*>(crow + t);
+                        const float4 va = *reinterpret_cast<const float4*>(vrow + t);
+                        const float4 vb = *reinterpret_cast<const float4*>(vrow + t + 4);
+                        const unsigned cwa[4] = {cw.x, cw.y, cw.z, cw.w};
+                        const float vv[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) {
+                            const int c = static_cast<int>((cwa[u >> 1] >> (16 * (u & 1))) & 0xffffu);
+                            fma_vec(vv[u], *reinterpret_cast<const float4*>(xcol + c * TN), acc);
+                        }
+                    }
+                    for (; t < cnt; ++t)
+                        fma_vec(vrow[t], *reinterpret_cast<const float4*>(xcol + crow[t] * TN), acc);
+                } else {
 #pragma unroll 4
-                for (; t + 1 < cnt; t += 2) {
-                    const int4 e = my4[t >> 1];
-                    const float4 x0 = *reinterpret_cast<const float4*>(xcol + e.x * TN);
-                    const float4 x1 = *reinterpret_cast<const float4*>(xcol + e.z * TN);
-                    fma_vec(__int_as_float(e.y), x0, acc);
-                    fma_vec(__int_as_float(e.w), x1, acc);
-                }
-                if (t < cnt) {
-                    const int2 e = my[t];
-                    const float4 x = *reinterpret_cast<const float4*>(xcol + e.x * TN);
-                    fma_vec(__int_as_float(e.y), x, acc);
+                    for (; t + 1 < cnt; t += 2) {
+                        const int4 e = my4[t >> 1];
+                        const float4 x0 = *reinterpret_cast<const float4*>(xcol + e.x * TN);
+                        const float4 x1 = *reinterpret_cast<const float4*>(xcol + e.z * TN);
+                        fma_vec(__int_as_float(e.y), x0, acc);
+                        fma_vec(__int_as_float(e.w), x1, acc);
+                    }
+                    if (t < cnt) {
+                        const int2 e = my[t];
+                        const float4 x = *reinterpret_cast<const float4*>(xcol + e.x * TN);
+                        fma_vec(__int_as_float(e.y), x, acc);
+                    }
                 }
                 __syncwarp();
             }
@@ -947,7 +980,12 @@ int launch_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, c
     const int nbox = static_cast<int>((K + kXsBoxRows - 1) / kXsBoxRows);
     const size_t smem = static_cast<size_t>(nbox) * kXsBoxRows * TN * 4 +
                         static_cast<size_t>(kXsWarps) * RPW * (xs_ch<LPR>() + 2) * sizeof(int2);
-    if (cudaFuncSetAttribute(spmm_xs_kernel<LPR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    // Packed (16-bit column) staging by default; SPARSECORE_B200_XS_PACK=0
+    // keeps (col, value) pairs (tests and measurements).
+    const char* pk = std::getenv("SPARSECORE_B200_XS_PACK");
+    const bool pack = !(pk != nullptr && pk[0] == '0') && K < 65536;
+    auto kern = pack ? spmm_xs_kernel<LPR, true> : spmm_xs_kernel<LPR, false>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
         return -1;
     const int row_chunks = (M + ROWS_PER_ITEM - 1) / ROWS_PER_ITEM;
@@ -961,7 +999,7 @@ int launch_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, c
     const int64_t per_cta = (n_items + grid - 1) / grid;
     grid = (n_items + per_cta - 1) / per_cta;
     note_kernel("spmm_xs_kernel");
-    spmm_xs_kernel<LPR><<<static_cast<unsigned>(grid), xs_threads<LPR>(), smem, s>>>(
+    kern<<<static_cast<unsigned>(grid), xs_threads<LPR>(), smem, s>>>(
         map, M, N, W->row_start, W->row_nnz, W->col_indices, W->values, Y, epi, nbox, row_chunks,
         n_items, per_cta, status);
     SL_RETURN_IF_LAUNCH_FAILED("sl_spmm_fwd (x-stationary)");

@@ -159,16 +159,21 @@ def test_transpose_involution_and_padding_ratio():
         W.transpose(padding_ratio=-1.0)
 
 
+@pytest.mark.parametrize("pack", ["1", "0"])
 @pytest.mark.parametrize("path", ["rows", "xs", "xs32", "xs64"])
-def test_forward_paths_and_sddmm_variants_vs_oracle(path, monkeypatch):
+def test_forward_paths_and_sddmm_variants_vs_oracle(path, pack, monkeypatch):
     """Both forward decompositions (row-gather and X-stationary with 128-,
-    64- and 32-column tiles), the lane and quad SDDMM kernels, ragged row lengths (one
-    dense row among sparse ones, empty rows) and column counts around every
-    dispatch threshold (partial last tiles included)."""
+    64- and 32-column tiles, with packed 16-bit-column or pair staging), the
+    lane and quad SDDMM kernels, ragged row lengths (one dense row among
+    sparse ones, empty rows) and column counts around every dispatch
+    threshold (partial last tiles included)."""
     import sparsecore_b200 as sl
     from oracle import oracle as O
     from sparsecore_b200 import ops
 
+    if path == "rows" and pack == "0":
+        pytest.skip("staging form applies to the X-stationary kernel only")
+    monkeypatch.setenv("SPARSECORE_B200_XS_PACK", pack)
     monkeypatch.setenv("SPARSECORE_B200_FWD", "xs" if path.startswith("xs") else path)
     if path in ("xs32", "xs64"):  # default: the widest tile that fits (here 64 for W, 128 for W^T)
         monkeypatch.setenv("SPARSECORE_B200_XS_TN", path[2:])
