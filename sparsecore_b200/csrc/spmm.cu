@@ -887,15 +887,16 @@ spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
             for (int base = 0; base < maxnn; base += kXsCh) {
                 if constexpr (PACK) {
                     // Packed staging: per row kXsCh values, then kXsCh 16-bit
-                    // columns (K < 65536), so 8 slots cost three 128-bit
-                    // reads instead of four.
+                    // X-tile offsets col * TN (below 65536: the K x TN tile
+                    // fits in shared memory), so 8 slots cost three 128-bit
+                    // reads instead of four and no lane multiplies.
 #pragma unroll
                     for (int it = 0; it < SlotStager<LPR, kXsCh, XST>::ITER; ++it) {
                         const int idx = it * 32 + lane;
                         float* rv = reinterpret_cast<float*>(st + (idx / kXsCh) * XST);
                         rv[idx % kXsCh] = sg.v[it];
                         reinterpret_cast<unsigned short*>(rv + kXsCh)[idx % kXsCh] =
-                            static_cast<unsigned short>(sg.c[it]);
+                            static_cast<unsigned short>(sg.c[it] * TN);
                     }
                 } else {
                     sg.store(st);
@@ -916,11 +917,11 @@ spmm_xs_kernel(const __grid_constant__ CUtensorMap xmap, int M, int64_t N,
 #pragma unroll
                         for (int u = 0; u < 8; ++u) {
                             const int c = static_cast<int>((cwa[u >> 1] >> (16 * (u & 1))) & 0xffffu);
-                            fma_vec(vv[u], *reinterpret_cast<const float4*>(xcol + c * TN), acc);
+                            fma_vec(vv[u], *reinterpret_cast<const float4*>(xcol + c), acc);
                         }
                     }
                     for (; t < cnt; ++t)
-                        fma_vec(vrow[t], *reinterpret_cast<const float4*>(xcol + crow[t] * TN), acc);
+                        fma_vec(vrow[t], *reinterpret_cast<const float4*>(xcol + crow[t]), acc);
                 } else {
 #pragma unroll 4
                     for (; t + 1 < cnt; t += 2) {
@@ -983,7 +984,7 @@ int launch_xs(const sl_csr* W, const float* X, int64_t K, int64_t N, float* Y, c
     // Packed (16-bit column) staging by default; SPARSECORE_B200_XS_PACK=0
     // keeps (col, value) pairs (tests and measurements).
     const char* pk = std::getenv("SPARSECORE_B200_XS_PACK");
-    const bool pack = !(pk != nullptr && pk[0] == '0') && K < 65536;
+    const bool pack = !(pk != nullptr && pk[0] == '0') && K * TN < 65536;
     auto kern = pack ? spmm_xs_kernel<LPR, true> : spmm_xs_kernel<LPR, false>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
