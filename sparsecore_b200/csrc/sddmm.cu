@@ -599,8 +599,8 @@ sddmm_tiled_kernel(const __grid_constant__ CUtensorMap dymap, const __grid_const
 // stream over the slot arrays: one warp per row writes the row's whole
 // capacity (live slots and zeroed padding) with coalesced loads of the
 // column indices and coalesced stores, X gathered through L1.  A warp keeps
-// the next round's column loads in flight while it gathers and stores the
-// current one (U strips of 32 slots per round), so each SM has tens of KB of
+// the next group's column loads in flight while it gathers and stores the
+// current one (U strips of 32 slots per group), so each SM has tens of KB of
 // loads outstanding.
 constexpr int kN1U = 8;
 __global__ void __launch_bounds__(256)
@@ -620,7 +620,7 @@ sddmm_n1_kernel(int M, const int32_t* __restrict__ row_start, const int32_t* __r
             c[u] = k < nn ? __ldg(cols + rs + k) : -1;
         }
         for (int k0 = 0; k0 < cp; k0 += 32 * kN1U) {
-            int cn[kN1U];  // next round's columns, in flight during this round's work
+            int cn[kN1U];  // the next group of strips' columns, in flight while this group is gathered
 #pragma unroll
             for (int u = 0; u < kN1U; ++u) {
                 const int k = k0 + 32 * (kN1U + u) + lane;
