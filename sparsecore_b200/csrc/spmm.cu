@@ -779,9 +779,18 @@ int dispatch_fwd(const sl_csr* W, const float* X, int64_t N, float* Y, cudaStrea
             if (t == 32) return launch_fwd<VEC, 8, 1>(W, X, N, Y, s, epi);
             if (t == 64) return launch_fwd<VEC, 16, 1>(W, X, N, Y, s, epi);
             if (t == 128) return launch_fwd<VEC, 32, 1>(W, X, N, Y, s, epi);
+            if (t == 256) return launch_fwd<VEC, 32, 2>(W, X, N, Y, s, epi);
         }
     }
-    if (nv >= 64) return launch_fwd<VEC, 32, 2>(W, X, N, Y, s, epi);
+    // 256-column tiles, or 128 when that leaves fewer than about four
+    // warps' items per SM (small layers: the work per warp is a serial walk
+    // of its row's slots, so more, narrower items finish sooner; config 1,
+    // 256 x 784 at N = 256, measured 18.0 -> 12.1 us).
+    if (nv >= 64) {
+        const int64_t items256 = W->nrows * ((N + 255) / 256);
+        if (items256 < 4LL * num_sms()) return launch_fwd<VEC, 32, 1>(W, X, N, Y, s, epi);
+        return launch_fwd<VEC, 32, 2>(W, X, N, Y, s, epi);
+    }
     if (nv > 16) return launch_fwd<VEC, 32, 1>(W, X, N, Y, s, epi);
     if (nv > 8) return launch_fwd<VEC, 16, 1>(W, X, N, Y, s, epi);
     if (nv > 4) return launch_fwd<VEC, 8, 1>(W, X, N, Y, s, epi);
