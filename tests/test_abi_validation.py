@@ -48,6 +48,23 @@ def test_spmm_and_sddmm_validation(lib):
     assert lib.sl_sddmm_dw(ref(csr()), None, BAD, 3, BAD, None) == N.SL_ERR_INVALID
 
 
+def test_fused_epilogue_and_bias_transpose_validation(lib):
+    ref = ctypes.byref
+    # activation code out of range; an activation without H
+    assert lib.sl_spmm_fwd_act(ref(csr()), BAD, 5, 3, None, 3, BAD, BAD, None) == N.SL_ERR_INVALID
+    assert "act must be" in err(lib)
+    assert lib.sl_spmm_fwd_act(ref(csr()), BAD, 5, 3, None, 2, BAD, None, None) == N.SL_ERR_INVALID
+    assert "NULL H" in err(lib)
+    assert lib.sl_spmm_fwd_act(ref(csr()), BAD, 6, 3, None, 0, BAD, None, None) == N.SL_ERR_INVALID
+    assert "Inner dimensions must match for matmul" in err(lib)
+    assert lib.sl_spmm_fwd_gelu(ref(csr()), BAD, 5, 3, BAD, None, None) == N.SL_ERR_INVALID
+    # the bias transpose: NULL bias, in place, negative shape
+    assert lib.sl_transpose_bias_f32(BAD, 4, 4, None, N.P(2), None) == N.SL_ERR_INVALID
+    assert "NULL bias" in err(lib)
+    assert lib.sl_transpose_bias_f32(BAD, 4, 4, BAD, BAD, None) == N.SL_ERR_INVALID
+    assert lib.sl_transpose_bias_f32(BAD, -1, 4, BAD, N.P(2), None) == N.SL_ERR_INVALID
+
+
 def test_layout_and_transpose_validation(lib):
     ref = ctypes.byref
     assert lib.sl_transpose_count(ref(csr(ncols=100000)), 1.2, BAD, BAD, BAD, BAD, BAD, None) \
