@@ -106,3 +106,60 @@ def test_graph_variants_for_rigl_capture(capture):
     # clone-free graph per topology (1, 3, 6, 9) plus the cloning one before
     # each update (2, 5, 8).
     assert gs.captures == (4 if capture == "every_step" else 7)
+
+
+class _FusedFFN(torch.nn.Module):
+    """Biased FFN pair through sparse_mlp (bias and GELU in the first
+    layer's forward kernel, the second bias in the output transpose)."""
+
+    def __init__(self):
+        import sparsecore_b200 as sl
+
+        super().__init__()
+        self.fc1 = sl.SparseLinear(64, 96, sparsity=0.8)
+        self.fc2 = sl.SparseLinear(96, 10, sparsity=0.7)
+
+    def forward(self, x):
+        import sparsecore_b200 as sl
+
+        return sl.sparse_mlp(x, self.fc1, self.fc2, "gelu")
+
+
+def test_graph_replay_of_fused_biased_ffn_matches_eager():
+    import sparsecore_b200 as sl
+    from sparsecore_b200.graph import GraphedStep
+
+    def setup():
+        torch.manual_seed(0)
+        model = _FusedFFN()
+        algo = sl.SET(sparsity=0.8, drop_fraction=0.3, update_freq=4, seed=1)
+        opt = torch.optim.SGD(model.parameters(), lr=0.05)
+        g = torch.Generator().manual_seed(9)
+        x = torch.randn(300, 64, generator=g).to(dev())
+        y = torch.randint(0, 10, (300,), generator=g).to(dev())
+        model.apply(algo)
+
+        def train(xb, yb):
+            opt.zero_grad(set_to_none=True)
+            loss = torch.nn.functional.cross_entropy(model(xb), yb)
+            loss.backward()
+            opt.step()
+            return loss
+
+        return algo, train, x, y, model
+
+    algo, train, x, y, model = setup()
+    eager = []
+    for _ in range(9):
+        eager.append(float(train(x, y).item()))
+        algo.step()
+    algo2, train2, x2, y2, model2 = setup()
+    train2(x2, y2)
+    algo2.step()
+    gs = GraphedStep(model2, train2, (x2, y2))
+    graphed = [eager[0]]
+    for _ in range(8):
+        graphed.append(float(gs().item()))
+        algo2.step()
+    assert graphed == eager
+    assert torch.equal(model.fc1.bias, model2.fc1.bias) and torch.equal(model.fc2.bias, model2.fc2.bias)
