@@ -19,6 +19,7 @@ from .layout import PaddedCSR, transpose_with_perm
 from .ops import critical_path_stream, set_async_weight_grad, spmm
 from .nn import SparseLinear, sparse_mlp
 from .router import SparsityAlgorithm, Static, DynamicSparsityAlgorithm, SET, RigL, dense_grad
+from . import torch_ops  # registers torch.ops.sparselab.spmm_fwd / sddmm_dw
 
 __all__ = [
     "PaddedCSR",
